@@ -1,0 +1,136 @@
+"""Generate the golden fixtures that pin ``oracle/`` to the reference itself.
+
+Run in a checkout that has the reference repository available (default
+``/root/reference``; override with ``TJ_REFERENCE_ROOT``)::
+
+    python tests/golden/make_golden.py
+
+It imports the reference's own modules -- ``torch_transformer_benchmark``
+(``BaselineTransformer``, ``generate_random_case``) and
+``src.implementations.poly_reference`` / ``poly_guard`` -- runs them on the CPU
+and writes small ``.npz`` files next to this script.  The reference is never
+needed at test time: ``tests/test_oracle_golden.py`` only reads these files.
+
+Fixtures
+--------
+``model_<name>.npz``  seeded model output for a configuration (full output for
+                      tiny shapes, a fixed random subset of rows for larger
+                      ones), the generated input's checksum and lengths.
+``poly_<name>.npz``   ``poly_linear_attention`` output (compute/state float32)
+                      for seeded q/k/v, plus the guard's sigma estimate.
+"""
+
+from __future__ import annotations
+
+import importlib
+import json
+import os
+import sys
+from pathlib import Path
+
+import numpy as np
+import torch
+
+HERE = Path(__file__).resolve().parent
+REF = Path(os.environ.get("TJ_REFERENCE_ROOT", "/root/reference"))
+
+# name: (B, N, d, H, F, L, causal, padding_ratio, linear_scale, rows_kept or None=all)
+MODEL_CASES = {
+    "tiny_causal": (2, 48, 64, 4, 96, 2, True, 0.5, 1.0, None),
+    "tiny_noncausal": (3, 40, 32, 2, 64, 1, False, 0.3, 1.0, None),
+    "tiny_scaled": (2, 64, 64, 2, 128, 1, True, 0.0, 0.5, None),
+    "c1": (4, 512, 256, 8, 1024, 2, True, 0.5, 1.0, 96),
+    "c3_b4": (4, 256, 512, 8, 2048, 4, True, 0.75, 1.0, 64),
+}
+MODEL_SEEDS = (1234, 1235)
+
+
+def _import_reference():
+    sys.path.insert(0, str(REF))
+    ttb = importlib.import_module("torch_transformer_benchmark")
+    poly_ref = importlib.import_module("src.implementations.poly_reference")
+    guard = importlib.import_module("src.implementations.poly_guard")
+    return ttb, poly_ref, guard
+
+
+def _model_fixture(ttb, name, spec):
+    b, n, d, h, f, layers, causal, pr, lscale, keep = spec
+    cfg = ttb.TransformerConfig(b, n, d, h, f, layers, causal)
+    torch.manual_seed(1234)
+    model = ttb.BaselineTransformer(cfg).eval()
+    if lscale != 1.0:
+        with torch.no_grad():
+            for mod in model.modules():
+                if isinstance(mod, torch.nn.Linear):
+                    mod.weight.mul_(lscale)
+                    mod.bias.mul_(lscale)
+    out = {"config": np.array([b, n, d, h, f, layers, int(causal)], dtype=np.int64),
+           "padding_ratio": np.float64(pr), "linear_scale": np.float64(lscale),
+           "seeds": np.array(MODEL_SEEDS, dtype=np.int64)}
+    rng = np.random.default_rng(7)
+    for seed in MODEL_SEEDS:
+        x, mask = ttb.generate_random_case(cfg, torch.device("cpu"), torch.float32, seed, pr, 1.0)
+        with torch.inference_mode():
+            y = model(x, mask)
+        rows = np.arange(b * n) if keep is None else np.sort(rng.choice(b * n, size=keep, replace=False))
+        out[f"rows_{seed}"] = rows.astype(np.int64)
+        out[f"y_{seed}"] = y.reshape(b * n, d).numpy()[rows]
+        out[f"lengths_{seed}"] = mask.sum(1).numpy().astype(np.int64)
+        out[f"xsum_{seed}"] = np.array([x.double().sum().item(), x.double().abs().sum().item()])
+        out[f"x0_{seed}"] = x.reshape(b * n, d).numpy()[rows[:4]]
+    # A mask with interior holes (not right padding) exercises the general key mask.
+    if name == "tiny_causal":
+        x, _ = ttb.generate_random_case(cfg, torch.device("cpu"), torch.float32, 99, 0.0, 1.0)
+        g = torch.Generator().manual_seed(5)
+        mask = torch.rand(b, n, generator=g) > 0.3
+        mask[:, 0] = True
+        x = x.masked_fill(~mask[..., None], 0)
+        with torch.inference_mode():
+            y = model(x, mask)
+        out["general_mask"] = mask.numpy()
+        out["general_y"] = y.reshape(b * n, d).numpy()
+    np.savez_compressed(HERE / f"model_{name}.npz", **out)
+
+
+# name: (B, H, N, D, chunk, exact_prefix, sigma)
+POLY_CASES = {
+    "d32": (1, 2, 512, 32, 128, 128, 0.334),
+    "d64": (1, 2, 384, 64, 128, 128, 0.334),
+    "d64_taylor": (1, 1, 320, 64, 64, 0, None),
+}
+
+
+def _poly_fixture(poly_ref, guard, name, spec):
+    b, h, n, dh, chunk, prefix, sigma = spec
+    gen = torch.Generator().manual_seed(0)
+    q = torch.randn(b, h, n, dh, generator=gen) * 0.577
+    k = torch.randn(b, h, n, dh, generator=gen) * 0.577
+    v = torch.randn(b, h, n, dh, generator=gen) * 0.577
+    scale = dh ** -0.5
+    y = poly_ref.poly_linear_attention(q, k, v, scale, chunk=chunk, exact_prefix=prefix,
+                                       sigma=sigma, state_dtype=torch.float32,
+                                       compute_dtype=torch.float32)
+    est = guard.estimate_sigma(q, k, scale)
+    c = poly_ref.hermite_coefficients(sigma)
+    np.savez_compressed(HERE / f"poly_{name}.npz", spec=np.array([b, h, n, dh, chunk, prefix]),
+                        sigma=np.float64(-1.0 if sigma is None else sigma), y=y.numpy(),
+                        sigma_est=np.float64(est), coeffs=np.array(c, dtype=np.float64))
+
+
+def main():
+    ttb, poly_ref, guard = _import_reference()
+    torch.set_num_threads(min(8, os.cpu_count() or 1))
+    for name, spec in MODEL_CASES.items():
+        _model_fixture(ttb, name, spec)
+        print("model", name)
+    for name, spec in POLY_CASES.items():
+        _poly_fixture(poly_ref, guard, name, spec)
+        print("poly", name)
+    meta = {"reference_root": str(REF), "torch": torch.__version__,
+            "model_cases": {k: list(v) for k, v in MODEL_CASES.items()},
+            "poly_cases": {k: list(v) for k, v in POLY_CASES.items()}}
+    (HERE / "MANIFEST.json").write_text(json.dumps(meta, indent=1) + "\n")
+
+
+if __name__ == "__main__":
+    main()
