@@ -1,0 +1,376 @@
+#!/usr/bin/env python3
+"""Forward-pass benchmark of the B200 encoder on one BASELINE workload.
+
+    python bench.py [--gpus N --steps K --warmup W] [--config C2] [--impl b200|reference]
+
+A step is one forward of the workload's batch (rank-local shard when N > 1).
+Default workload: C2 (B=16, N=2048, d=1024, 16 heads, FFN 4096, 4 layers,
+causal, lengths uniform in [1024, 2048]) -- BASELINE.json's ``configs[1]``.
+For N > 1 the batch is split over ranks (cost-balanced), so total work is
+fixed: ``scaling: strong``; ``value`` is the max-over-ranks latency.
+
+One JSON line on rank 0.  ``value`` = device-timed forward latency (inputs
+resident in HBM, CUDA events on the launching stream, barrier + synchronize
+on both sides).  ``e2e`` = the same forward through the public API
+(``DispatchingTransformer.forward``) including the host->device copy of x and
+the mask from pinned memory and the device->host copy of the output.
+``roofline`` = the dominant kernel class measured live with per-launch CUDA
+events (libtj's profiler) in a second pass over the same inputs.
+``cpu_baseline`` = the oracle (an FP32 restatement of the reference dense
+model) on the host cores for one sample, extrapolated to the batch by
+algorithmic work.  ``--impl reference`` times that same CPU model as the
+reference arm.
+"""
+
+from __future__ import annotations
+
+import argparse
+import ctypes
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import torch
+import torch.distributed as dist
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+from techjam_b200 import _lib  # noqa: E402
+from techjam_b200.dispatcher import DispatchingTransformer  # noqa: E402
+from techjam_b200.harness import CONFIGS, generate_random_case, seeded_model, valid_lengths, work  # noqa: E402
+
+SEED = 1234 + 100000  # the reference harness's timing input seed (torch_transformer_benchmark.py:459-466)
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+# DRAM bytes per launch from ncu captures (profiles/*.md), keyed (workload, kernel class).
+NCU_TRAFFIC_BYTES: dict = {}
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="C2")
+    ap.add_argument("--route", choices=("exact", "poly", "auto"), default="auto")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-repeats", type=int, default=2)
+    return ap.parse_args()
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            d = json.loads(p.read_text())
+            return {k: float(d[k]) for k in FALLBACK_PEAKS}, "measured"
+        except Exception:
+            pass
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def shard_samples(lengths, world, rank, cfg):
+    """Longest-processing-time assignment of samples to ranks by algorithmic cost."""
+    d, F_ = cfg.d_model, cfg.ffn_dim
+    cost = [(l * (4 * d * d + 2 * d * F_) + d * l * (l + 1), i) for i, l in enumerate(lengths)]
+    loads = [0.0] * world
+    owner = {}
+    for c, i in sorted(cost, reverse=True):
+        r = min(range(world), key=lambda j: (loads[j], j))
+        loads[r] += c
+        owner[i] = r
+    return sorted(i for i in owner if owner[i] == rank)
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    FIELDS = ("index,pci.bus_id,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.device_index = device_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-f", self.path], stdout=subprocess.DEVNULL,
+                                         stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if self.proc is None or not self.path or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        try:
+            bus = torch.cuda.get_device_properties(self.device_index).pci_bus_id
+        except Exception:
+            bus = None
+        rows = []
+        for line in Path(self.path).read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 10:
+                continue
+            rows.append(parts)
+        os.unlink(self.path)
+        if bus is not None:
+            mine = [r for r in rows if r[1].lower().endswith(str(bus).lower()[-7:])]
+            rows = mine or rows
+        names = ["active", "hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        sm, smax, reasons = [], [], set()
+        for r in rows:
+            try:
+                sm.append(float(r[2]))
+                smax.append(float(r[3]))
+            except ValueError:
+                continue
+            for n, v in zip(names[1:], r[6:10]):
+                if v.strip().lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        loaded = [s for s in sm if s >= 0.5 * max(sm)] or sm
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": max(smax), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ CPU baseline (oracle)
+def cpu_reference_ms(cfg, wl, x_full, mask_full, lengths, steps, warmup, sample_index=None):
+    """Time the oracle (FP32 restatement of the reference dense model) on the host
+    CPU for single samples; return full-batch-equivalent ms per step (scaled by
+    algorithmic work), the thread count and a sample description."""
+    from oracle.reference_model import OracleEncoder  # CPU-baseline leg only
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    model = seeded_model(OracleEncoder, cfg, 1234, wl.linear_scale)
+    total = work(cfg, lengths)
+    total_flops = total["gemm_flops"] + total["attn_flops"]
+    per_step = []
+    idx = list(range(cfg.batch_size)) if sample_index is None else [sample_index]
+    with torch.inference_mode():
+        for s in range(warmup + steps):
+            i = idx[s % len(idx)]
+            x = x_full[i:i + 1].cpu()
+            m = mask_full[i:i + 1].cpu()
+            t0 = time.perf_counter_ns()
+            model(x, m)
+            t1 = time.perf_counter_ns()
+            if s >= warmup:
+                one = work(cfg, [lengths[i]])
+                per_step.append((t1 - t0) / 1e6 * total_flops / (one["gemm_flops"] + one["attn_flops"]))
+    return statistics.mean(per_step), threads, idx
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    wl = CONFIGS[args.config]
+    cfg = wl.config
+    x, mask = generate_random_case(cfg, torch.device("cpu"), torch.float32, SEED, wl.padding_ratio)
+    lengths = valid_lengths(mask, cfg.batch_size, cfg.seq_len)
+    ms, threads, idx = cpu_reference_ms(cfg, wl, x, mask, lengths, args.steps, args.warmup)
+    line = {
+        "impl": "reference", "metric": "fwd_latency_ms", "value": round(ms, 3), "unit": "ms", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": False,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic (reference generator, seed 101234)",
+        "config": {"workload": wl.name, "batch": cfg.batch_size, "seq_len": cfg.seq_len, "d_model": cfg.d_model,
+                   "heads": cfg.num_heads, "ffn_dim": cfg.ffn_dim, "layers": cfg.num_layers,
+                   "padding_ratio": wl.padding_ratio},
+        "cpu_baseline": {"value": round(ms, 3), "unit": "ms", "cores": threads, "kind": "port",
+                         "sample": (f"one B=1 sample per step (cycling samples 0..{cfg.batch_size - 1}), "
+                                    f"oracle FP32 dense model on host CPU, scaled to the full batch by algorithmic flops")},
+        "e2e": {"value": round(ms, 3), "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------------ B200 arm
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+
+    wl = CONFIGS[args.config]
+    cfg = wl.config
+    x_full, mask_full = generate_random_case(cfg, dev, torch.float32, SEED, wl.padding_ratio)
+    lengths = valid_lengths(mask_full, cfg.batch_size, cfg.seq_len)
+    mine = shard_samples(lengths, world, rank, cfg)
+    sel = torch.tensor(mine, device=dev, dtype=torch.long)
+    x = x_full.index_select(0, sel).contiguous()
+    mask = mask_full.index_select(0, sel).contiguous()
+    my_lengths = [lengths[i] for i in mine]
+    model = seeded_model(DispatchingTransformer, cfg, 1234, wl.linear_scale, attention_route=args.route).to(dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    with torch.inference_mode():
+        for _ in range(args.warmup):
+            model(x, mask)
+        torch.cuda.synchronize(dev)
+        if model.device_error() != 0:
+            raise RuntimeError("device error during warm-up")
+        # ---- timed region: K forwards, inputs resident in HBM
+        n0 = ctypes.c_longlong()
+        _lib.call("tj_launch_count", model._handle.ptr, ctypes.byref(n0))
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        torch.cuda.synchronize(dev)
+        with ClockSampler(local) as clocks:
+            start.record(stream)
+            for _ in range(args.steps):
+                model(x, mask)
+            end.record(stream)
+            torch.cuda.synchronize(dev)
+        barrier()
+        ms_local = start.elapsed_time(end) / args.steps
+        n1 = ctypes.c_longlong()
+        _lib.call("tj_launch_count", model._handle.ptr, ctypes.byref(n1))
+        launches = int(n1.value - n0.value)
+        ms = max_over_ranks(ms_local)
+
+        # ---- per-kernel pass (event pairs around every launch)
+        per_fwd = 7 * cfg.num_layers + 3
+        _lib.call("tj_profile_begin", model._handle.ptr, per_fwd * args.steps)
+        for _ in range(args.steps):
+            model(x, mask)
+        kms = (ctypes.c_double * 9)()
+        kcnt = (ctypes.c_longlong * 9)()
+        _lib.call("tj_profile_end", model._handle.ptr, kms, kcnt)
+        if model.device_error() != 0:
+            raise RuntimeError("device error during timing")
+
+        # ---- end to end through the public API with host buffers
+        e2e = None
+        if not args.no_e2e:
+            xh = x.cpu().pin_memory()
+            mh = mask.cpu().pin_memory()
+            outh = torch.empty(x.shape, dtype=torch.float32).pin_memory()
+            for _ in range(max(1, args.warmup)):
+                outh.copy_(model(xh.to(dev, non_blocking=True), mh.to(dev, non_blocking=True)), non_blocking=True)
+            torch.cuda.synchronize(dev)
+            barrier()
+            s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s2.record(stream)
+            for _ in range(args.steps):
+                y = model(xh.to(dev, non_blocking=True), mh.to(dev, non_blocking=True))
+                outh.copy_(y, non_blocking=True)
+            e2.record(stream)
+            torch.cuda.synchronize(dev)
+            barrier()
+            e2e_ms = max_over_ranks(s2.elapsed_time(e2) / args.steps)
+            e2e = {"value": round(e2e_ms, 4), "unit": "ms",
+                   "h2d_bytes_per_step": int(xh.numel() * 4 + mh.numel()),
+                   "d2h_bytes_per_step": int(outh.numel() * 4)}
+
+    # aggregate per-kernel timing across ranks (max ms per class)
+    kms_l = [max_over_ranks(kms[i] / args.steps) for i in range(9)]
+    peaks, peak_src = load_peaks()
+    w_all = work(cfg, lengths)
+    w_mine = work(cfg, my_lengths)
+    names = _lib.KERNEL_CLASSES
+    flops_of = {"gemm_qkv": w_mine["gemm_qkv_flops"], "gemm_out": w_mine["gemm_out_flops"],
+                "gemm_ffn_in": w_mine["gemm_ffn_in_flops"], "gemm_ffn_out": w_mine["gemm_ffn_out_flops"],
+                "attention": w_mine["attn_flops"]}
+    total_k = sum(kms_l) or 1.0
+    kernels = {}
+    for i, n in enumerate(names):
+        if kcnt[i] == 0:
+            continue
+        entry = {"ms_per_step": round(kms_l[i], 4), "share": round(kms_l[i] / total_k, 4),
+                 "launches_per_step": kcnt[i] // args.steps}
+        if n in flops_of and kms_l[i] > 0:
+            entry["tflops"] = round(flops_of[n] / (kms_l[i] * 1e-3) / 1e12, 1)
+        kernels[n] = entry
+    dom = max((n for n in kernels if n in flops_of), key=lambda n: kernels[n]["ms_per_step"])
+    di = names.index(dom)
+    per_launch_ms = kms_l[di] / max(1, kcnt[di] // args.steps)
+    per_launch_flops = flops_of[dom] / max(1, kcnt[di] // args.steps)
+    achieved = per_launch_flops / (per_launch_ms * 1e-3) / 1e12
+    peak = peaks["bf16_tflops_sustained"]
+    traffic = NCU_TRAFFIC_BYTES.get((wl.name, dom))
+    attn_tflops = w_all["attn_flops"] / (max_over_ranks(kms[3] / args.steps) * 1e-3) / 1e12 if kcnt[3] else None
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cms, threads, idx = cpu_reference_ms(cfg, wl, x_full, mask_full, lengths, args.cpu_repeats, 1,
+                                             sample_index=0)
+        cpu = {"value": round(cms, 1), "unit": "ms", "cores": threads, "kind": "port",
+               "sample": (f"sample 0 (B=1, {lengths[0]} valid tokens) of the same workload, oracle FP32 dense "
+                          f"model on {threads} host threads, mean of {args.cpu_repeats} after 1 warm-up, "
+                          "scaled to the full batch by algorithmic flops")}
+
+    if rank == 0:
+        line = {
+            "metric": "fwd_latency_ms", "value": round(ms, 4), "unit": "ms", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": False, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f16 operands / f32 accumulate, f32 residual + interface",
+            "data": "synthetic (reference generator, seed 101234; seeded default-init weights)",
+            "config": {"workload": wl.name, "batch": cfg.batch_size, "seq_len": cfg.seq_len,
+                       "d_model": cfg.d_model, "heads": cfg.num_heads, "ffn_dim": cfg.ffn_dim,
+                       "layers": cfg.num_layers, "causal": cfg.causal, "padding_ratio": wl.padding_ratio,
+                       "linear_scale": wl.linear_scale, "route": args.route,
+                       "parallelism": f"batch-shard x{world}" if world > 1 else "single GPU",
+                       "l2": "inputs (x 134 MB) and per-step activations exceed the 126 MB L2"},
+            "throughput_tokens_per_s": round(w_all["tokens_valid"] / (ms * 1e-3), 1),
+            "attn_tflops": None if attn_tflops is None else round(attn_tflops, 1),
+            "attn_frac_of_peak": None if attn_tflops is None else round(attn_tflops / peak, 4),
+            "gemm_tflops": round(w_all["gemm_flops"] / (ms * 1e-3) / 1e12, 1),
+            "kernels": kernels,
+            "roofline": {"kernel": dom, "bound": "tensor", "achieved": round(achieved, 1), "peak": peak,
+                         "unit": "TFLOP/s", "frac": round(achieved / peak, 4), "traffic": traffic,
+                         "peak_source": f"{peak_src} bf16_tflops_sustained (fp16 dense rate)"},
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": launches,
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,185 @@
+/*
+ * techjam-b200 C ABI: forward pass of the reference's fixed pre-LN Transformer
+ * encoder on B200 (sm_100a).  Plain pointers and sizes only; every entry point
+ * returns a TjStatus and, on failure, leaves a message for tj_last_error().
+ * All device work is enqueued on the caller's stream (a cudaStream_t passed as
+ * void*); nothing here allocates device memory except tj_model_create /
+ * tj_model_load_* (packed weights, owned by the model).
+ *
+ * Reference interfaces replaced (paths inside the reference repository):
+ *   tj_model_create        BaselineTransformer.__init__ / TransformerConfig
+ *                          (torch_transformer_benchmark.py:29-56, 148-160) and the
+ *                          candidate factory CandidateSpec.model_factory
+ *                          (src/infra/candidate.py:15-39, src/dispatcher.py:267-293)
+ *   tj_model_load_layer    copy_model_weights -> load_state_dict
+ *   tj_model_load_final_norm   (torch_transformer_benchmark.py:203-213) plus the
+ *                          packed-QKV rebuild of PackedQKVSDPASelfAttention
+ *                          (src/implementations/sdpa.py:96-116)
+ *   tj_forward             BaselineTransformer.forward / DispatchingTransformer.forward
+ *                          (torch_transformer_benchmark.py:162-172; src/dispatcher.py:708-794)
+ *   tj_prepare_mask        classify_mask / _mask_kind (src/implementations/
+ *                          attention_routing.py:76-98; src/dispatcher.py:393-423),
+ *                          without the host synchronisation
+ *   tj_layernorm           nn.LayerNorm in BaselineTransformerBlock (:128,130,160)
+ *   tj_gemm_f16            the nn.Linear projections (:72-75, 131-132) with the
+ *                          fused epilogues of :118-121, 141-144
+ *   tj_attention_f16       BaselineSelfAttention.forward scores/softmax/PV (:97-116)
+ *                          and StridedSDPASelfAttention (src/implementations/sdpa.py:46-78)
+ */
+#ifndef TJ_H_
+#define TJ_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define TJ_API __attribute__((visibility("default")))
+#else
+#define TJ_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum TjStatus {
+  TJ_OK = 0,
+  TJ_ERR_INVALID = 1,      /* bad argument (null pointer, shape mismatch, bad workspace) */
+  TJ_ERR_UNSUPPORTED = 2,  /* shape outside the kernels' envelope (e.g. head_dim) */
+  TJ_ERR_CUDA = 3,         /* CUDA runtime / driver error */
+  TJ_ERR_DEVICE = 4,       /* a kernel's bounded wait expired; see tj_device_error */
+  TJ_ERR_NO_DEVICE = 5     /* no sm_100 device is current */
+} TjStatus;
+
+/* Attention evaluation route for the forward pass. */
+typedef enum TjAttentionRoute {
+  TJ_ROUTE_EXACT = 0, /* exact causal/padded softmax attention (flash-style) */
+  TJ_ROUTE_POLY = 1,  /* guarded degree-2 polynomial route; falls back to exact
+                         when the fused score-range check fails */
+  TJ_ROUTE_AUTO = 2   /* poly for long causal unpadded sequences, exact otherwise */
+} TjAttentionRoute;
+
+typedef struct TjConfig {
+  int d_model;
+  int num_heads;
+  int ffn_dim;
+  int num_layers;
+  int causal;       /* nonzero: causal attention */
+  float layer_norm_eps; /* nn.LayerNorm default 1e-5 */
+} TjConfig;
+
+/* Device pointers to one block's FP32 parameters in nn.Linear layout
+   (weight [out_features, in_features] row-major). */
+typedef struct TjLayerParams {
+  const float* norm1_weight;
+  const float* norm1_bias;
+  const float* q_weight;
+  const float* q_bias;
+  const float* k_weight;
+  const float* k_bias;
+  const float* v_weight;
+  const float* v_bias;
+  const float* out_weight;
+  const float* out_bias;
+  const float* norm2_weight;
+  const float* norm2_bias;
+  const float* ffn_in_weight;
+  const float* ffn_in_bias;
+  const float* ffn_out_weight;
+  const float* ffn_out_bias;
+} TjLayerParams;
+
+typedef struct TjModel TjModel;
+
+TJ_API int tj_version(void);
+/* Message of the last failing call on this thread ("" if none). */
+TJ_API const char* tj_last_error(void);
+
+/* Creates a model on the current CUDA device; allocates its packed-weight
+   buffers and its device error word. */
+TJ_API int tj_model_create(const TjConfig* cfg, TjModel** out);
+TJ_API int tj_model_destroy(TjModel* model);
+/* Converts one block's FP32 parameters into the model's packed FP16 weights
+   ([3d, d] packed QKV, [d, d], [F, d], [d, F]) and FP32 biases / norms. */
+TJ_API int tj_model_load_layer(TjModel* model, int layer, const TjLayerParams* params, void* stream);
+TJ_API int tj_model_load_final_norm(TjModel* model, const float* weight, const float* bias, void* stream);
+
+/* Bytes of scratch tj_forward needs for [batch, seq_len] inputs.  The
+   workspace must be zero-filled before its first use (afterwards tj_forward
+   only ever writes finite values into it). */
+TJ_API int tj_workspace_bytes(const TjModel* model, int batch, int seq_len, size_t* bytes);
+
+/* out[B,S,d] = encoder(x[B,S,d]) with the reference's padding semantics:
+   valid_mask[B,S] (1 byte per token, nullable = all valid); padded output rows
+   are exactly 0.  x and out are FP32 device buffers and may not alias.
+   route: TjAttentionRoute. */
+TJ_API int tj_forward(TjModel* model, const float* x, const uint8_t* valid_mask, float* out, int batch, int seq_len,
+               int route, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Reads (synchronously) and clears the model's device error word: 0 if no
+   kernel's bounded wait expired since the last call. */
+TJ_API int tj_device_error(TjModel* model, int* code);
+
+/* ---- per-kernel timing (CUDA events recorded around each launch) ------- */
+
+typedef enum TjKernelClass {
+  TJ_K_PREP = 0,      /* mask -> lengths / live tiles */
+  TJ_K_LN = 1,        /* LayerNorm -> fp16 GEMM operand */
+  TJ_K_QKV = 2,       /* packed QKV GEMM (+ head scatter) */
+  TJ_K_ATTN = 3,      /* flash attention */
+  TJ_K_OUT = 4,       /* output projection GEMM (+ residual) */
+  TJ_K_FFN_IN = 5,    /* FFN-in GEMM (+ GELU) */
+  TJ_K_FFN_OUT = 6,   /* FFN-out GEMM (+ residual) */
+  TJ_K_LN_FINAL = 7,  /* final LayerNorm (fp32 out) */
+  TJ_K_POLY = 8,      /* polynomial-route kernels */
+  TJ_K_COUNT = 9
+} TjKernelClass;
+
+/* Start recording a CUDA-event pair around each of the next (at most)
+   max_launches kernel launches of this model. */
+TJ_API int tj_profile_begin(TjModel* model, int max_launches);
+/* Synchronises on the recorded events and writes, per TjKernelClass, the
+   summed device milliseconds and launch counts (arrays of TJ_K_COUNT). */
+TJ_API int tj_profile_end(TjModel* model, double* ms_by_class, long long* launches_by_class);
+/* Total kernels this model has launched (all classes, profiling or not). */
+TJ_API int tj_launch_count(TjModel* model, long long* count);
+
+/* ---- building blocks (same kernels the forward uses) ------------------- */
+
+/* lengths[b] = 1 + last valid position; general[b] = mask is not a prefix;
+   tile_list / n_live / tile_live describe the 128-row tiles of the flattened
+   [B*S] rows that hold at least one valid row.  mask may be null. */
+TJ_API int tj_prepare_mask(const uint8_t* mask, int batch, int seq_len, int* lengths, uint8_t* general, int* tile_list,
+                    int* n_live, uint8_t* tile_live, void* stream);
+
+/* Row-wise LayerNorm of x[rows, d] (FP32) into out (FP16 if out_fp16 else
+   FP32); rows outside the valid prefix (lengths/mask, rows = batch*seq_len)
+   are written as zeros (FP32 output: all of them; FP16: those in live tiles). */
+TJ_API int tj_layernorm(const float* x, const float* gamma, const float* beta, int batch, int seq_len, int d, float eps,
+                 void* out, int out_fp16, const int* lengths, const uint8_t* mask, const uint8_t* tile_live,
+                 void* stream);
+
+typedef enum TjEpilogue {
+  TJ_EPI_QKV = 0,     /* scatter bias-added fp16 columns into Q,K,V [B,H,S,hd] */
+  TJ_EPI_GELU = 1,    /* out16 = gelu_erf(acc + bias) */
+  TJ_EPI_RESID = 2,   /* out32 = resid + acc + bias (resid may alias out32) */
+  TJ_EPI_PLAIN16 = 3  /* out16 = acc + bias */
+} TjEpilogue;
+
+/* C[M,N] = A[M,K] (fp16, row-major) x W[N,K]^T (fp16, row-major) on tcgen05
+   with fp32 accumulation, over the live 128-row tiles of tile_list; invalid
+   rows (lengths/mask over rows = batch*seq_len) are written as zeros. */
+TJ_API int tj_gemm_f16(const void* a, const void* w, const float* bias, int batch, int seq_len, int n, int k, int epilogue,
+                void* out, const float* resid, void* q, void* k_out, void* v, int heads, const int* tile_list,
+                const int* n_live, const int* lengths, const uint8_t* mask, int* err, void* stream);
+
+/* ctx[B*S, H*hd] (fp16) = softmax(Q K^T * hd^-0.5 [+ causal/padding masks]) V
+   with Q,K,V fp16 [B,H,S,hd]; hd in {32, 64, 128}. */
+TJ_API int tj_attention_f16(const void* q, const void* k, const void* v, void* ctx, int batch, int heads, int seq_len,
+                     int head_dim, int causal, const int* lengths, const uint8_t* mask, const uint8_t* general,
+                     int* err, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TJ_H_ */

@@ -1,0 +1,614 @@
+// C ABI of techjam-b200: model object, packed weights, workspace carving,
+// tensor-map encoding and the forward-pass launch sequence.
+#include <cudaTypedefs.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/tj.h"
+#include "tj_attention.cuh"
+#include "tj_common.cuh"
+#include "tj_gemm.cuh"
+#include "tj_misc.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int status, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return status;
+}
+
+#define TJ_CUDA(call)                                                                       \
+  do {                                                                                      \
+    cudaError_t e_ = (call);                                                                \
+    if (e_ != cudaSuccess) return fail(TJ_ERR_CUDA, "%s: %s (%s:%d)", #call, cudaGetErrorString(e_), __FILE__, __LINE__); \
+  } while (0)
+
+#define TJ_CHECK(status) \
+  do {                   \
+    int s_ = (status);   \
+    if (s_ != TJ_OK) return s_; \
+  } while (0)
+
+// ------------------------------------------------------------------ device info
+struct DeviceInfo {
+  int sms = 0;
+  int major = 0;
+};
+std::mutex g_dev_mu;
+DeviceInfo g_dev[64];
+
+int device_info(DeviceInfo* out) {
+  int dev = 0;
+  TJ_CUDA(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lock(g_dev_mu);
+  if (dev < 0 || dev >= 64) return fail(TJ_ERR_NO_DEVICE, "device index %d out of range", dev);
+  if (g_dev[dev].sms == 0) {
+    cudaDeviceProp prop;
+    TJ_CUDA(cudaGetDeviceProperties(&prop, dev));
+    g_dev[dev].sms = prop.multiProcessorCount;
+    g_dev[dev].major = prop.major;
+  }
+  if (g_dev[dev].major != 10) return fail(TJ_ERR_NO_DEVICE, "device %d is sm_%d x, need sm_100", dev, g_dev[dev].major);
+  *out = g_dev[dev];
+  return TJ_OK;
+}
+
+// ------------------------------------------------------------------ tensor maps
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+int get_encoder() {
+  static std::once_flag once;
+  static int status = TJ_OK;
+  std::call_once(once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+    if (e != cudaSuccess || fn == nullptr || q != cudaDriverEntryPointSuccess) {
+      status = fail(TJ_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+      return;
+    }
+    g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  });
+  return g_encode ? TJ_OK : status;
+}
+
+// fp16 row-major [rows, cols] matrix, box [box_rows, box_cols], given swizzle.
+int make_map_f16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows,
+                 uint32_t box_cols, int swizzle_bytes) {
+  TJ_CHECK(get_encoder());
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) return fail(TJ_ERR_INVALID, "tensor base not 16-byte aligned");
+  if ((cols * 2) % 16 != 0) return fail(TJ_ERR_UNSUPPORTED, "row pitch %llu bytes not a multiple of 16", (unsigned long long)(cols * 2));
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {cols * 2};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUtensorMapSwizzle sw = swizzle_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                          : swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                                : CU_TENSOR_MAP_SWIZZLE_32B;
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(TJ_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return TJ_OK;
+}
+
+inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// ------------------------------------------------------------------ kernel launchers
+template <int BN, int EPI>
+int launch_gemm_bn(const CUtensorMap& ta, const CUtensorMap& tw, const tj::GemmParams& p, int sms, cudaStream_t st) {
+  using Cfg = tj::GemmCfg<BN>;
+  auto kern = tj::gemm_tc_kernel<BN, EPI>;
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev]) {
+    TJ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes));
+    attr_set[dev] = true;
+  }
+  const long long m_tiles = (p.M + tj::kGemmBM - 1) / tj::kGemmBM;
+  const long long n_tiles = (p.N + BN - 1) / BN;
+  const long long total = m_tiles * n_tiles;
+  const int grid = (int)std::min<long long>(total, sms);
+  if (grid <= 0) return TJ_OK;
+  kern<<<grid, Cfg::kThreads, Cfg::kSmemBytes, st>>>(ta, tw, p);
+  TJ_CUDA(cudaGetLastError());
+  return TJ_OK;
+}
+
+template <int EPI>
+int launch_gemm(const void* a, const void* w, const tj::GemmParams& p, int sms, cudaStream_t st) {
+  CUtensorMap ta, tw;
+  TJ_CHECK(make_map_f16(&ta, a, p.M, p.K, tj::kGemmBM, tj::kGemmBK, 128));
+  // Wide tiles when there are enough of them to fill the machine, else 128.
+  const long long m_tiles = (p.M + 127) / 128;
+  const bool wide = (p.N % 256 == 0) && (m_tiles * (p.N / 256) >= sms);
+  if (wide) {
+    TJ_CHECK(make_map_f16(&tw, w, p.N, p.K, 256, tj::kGemmBK, 128));
+    return launch_gemm_bn<256, EPI>(ta, tw, p, sms, st);
+  }
+  TJ_CHECK(make_map_f16(&tw, w, p.N, p.K, 128, tj::kGemmBK, 128));
+  return launch_gemm_bn<128, EPI>(ta, tw, p, sms, st);
+}
+
+int launch_gemm_epi(int epi, const void* a, const void* w, const tj::GemmParams& p, int sms, cudaStream_t st) {
+  switch (epi) {
+    case tj::kEpiQKV: return launch_gemm<tj::kEpiQKV>(a, w, p, sms, st);
+    case tj::kEpiGelu: return launch_gemm<tj::kEpiGelu>(a, w, p, sms, st);
+    case tj::kEpiResid: return launch_gemm<tj::kEpiResid>(a, w, p, sms, st);
+    case tj::kEpiPlain16: return launch_gemm<tj::kEpiPlain16>(a, w, p, sms, st);
+    default: return fail(TJ_ERR_INVALID, "unknown epilogue %d", epi);
+  }
+}
+
+template <int HD>
+int launch_attn_hd(const void* q, const void* k, const void* v, const tj::AttnParams& p, int B, cudaStream_t st) {
+  using Cfg = tj::AttnCfg<HD>;
+  CUtensorMap tq, tk, tv;
+  const uint64_t rows = (uint64_t)B * p.H * p.S;
+  TJ_CHECK(make_map_f16(&tq, q, rows, HD, 128, Cfg::kAtomCols, Cfg::kSw));
+  TJ_CHECK(make_map_f16(&tk, k, rows, HD, 128, Cfg::kAtomCols, Cfg::kSw));
+  TJ_CHECK(make_map_f16(&tv, v, rows, HD, 128, Cfg::kAtomCols, Cfg::kSw));
+  auto kern = tj::attn_fwd_kernel<HD>;
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev]) {
+    TJ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes));
+    attr_set[dev] = true;
+  }
+  dim3 grid((p.S + 127) / 128, B * p.H);
+  kern<<<grid, 192, Cfg::kSmemBytes, st>>>(tq, tk, tv, p);
+  TJ_CUDA(cudaGetLastError());
+  return TJ_OK;
+}
+
+int launch_attention(const void* q, const void* k, const void* v, int head_dim, const tj::AttnParams& p, int B,
+                     cudaStream_t st) {
+  if (B <= 0 || p.S <= 0) return TJ_OK;
+  if ((long long)B * p.H > 65535) return fail(TJ_ERR_UNSUPPORTED, "batch*heads %lld exceeds 65535", (long long)B * p.H);
+  switch (head_dim) {
+    case 32: return launch_attn_hd<32>(q, k, v, p, B, st);
+    case 64: return launch_attn_hd<64>(q, k, v, p, B, st);
+    case 128: return launch_attn_hd<128>(q, k, v, p, B, st);
+    default: return fail(TJ_ERR_UNSUPPORTED, "head_dim %d not supported (32, 64, 128)", head_dim);
+  }
+}
+
+int launch_layernorm(const float* x, const float* g, const float* b, void* out, bool f16, bool all_rows, int d,
+                     float eps, const tj::RowValidity& rv, const uint8_t* tile_live, cudaStream_t st) {
+  if (d % 4 != 0 || d > 4096) return fail(TJ_ERR_UNSUPPORTED, "LayerNorm width %d (need multiple of 4, <= 4096)", d);
+  if (rv.M == 0) return TJ_OK;
+  const int warps = 8;
+  const long long blocks = (rv.M + warps - 1) / warps;
+  if (blocks > 0x7fffffffLL) return fail(TJ_ERR_UNSUPPORTED, "too many rows");
+  const int vpl = (d / 4 + 31) / 32;
+#define TJ_LN(V)                                                                                              \
+  if (f16) {                                                                                                  \
+    if (all_rows) tj::layernorm_kernel<V, true, true><<<(unsigned)blocks, 256, 0, st>>>(x, g, b, out, d, eps, rv, tile_live); \
+    else tj::layernorm_kernel<V, true, false><<<(unsigned)blocks, 256, 0, st>>>(x, g, b, out, d, eps, rv, tile_live);         \
+  } else {                                                                                                    \
+    if (all_rows) tj::layernorm_kernel<V, false, true><<<(unsigned)blocks, 256, 0, st>>>(x, g, b, out, d, eps, rv, tile_live); \
+    else tj::layernorm_kernel<V, false, false><<<(unsigned)blocks, 256, 0, st>>>(x, g, b, out, d, eps, rv, tile_live);        \
+  }
+  if (vpl <= 1) { TJ_LN(1) }
+  else if (vpl <= 2) { TJ_LN(2) }
+  else if (vpl <= 4) { TJ_LN(4) }
+  else if (vpl <= 8) { TJ_LN(8) }
+  else { TJ_LN(32) }
+#undef TJ_LN
+  TJ_CUDA(cudaGetLastError());
+  return TJ_OK;
+}
+
+int launch_prepare(const uint8_t* mask, int B, int S, int* lengths, uint8_t* general, int* tile_list, int* n_live,
+                   uint8_t* tile_live, cudaStream_t st) {
+  tj::prep_lengths_kernel<<<B, 256, 0, st>>>(mask, S, lengths, general);
+  TJ_CUDA(cudaGetLastError());
+  tj::prep_tiles_kernel<<<1, 1024, 0, st>>>(lengths, B, S, tile_list, n_live, tile_live);
+  TJ_CUDA(cudaGetLastError());
+  return TJ_OK;
+}
+
+// ------------------------------------------------------------------ workspace layout
+struct Workspace {
+  int* lengths;
+  uint8_t* general;
+  int* tile_list;
+  int* n_live;
+  uint8_t* tile_live;
+  __half* act;  // [M, d]: LN output, then attention context (reused)
+  __half* q;
+  __half* k;
+  __half* v;    // [B, H, S, hd] each
+  __half* ff;   // [M, F]
+};
+
+size_t carve(const TjConfig& c, int B, int S, uint8_t* base, Workspace* w) {
+  const size_t M = (size_t)B * S;
+  const size_t tiles = (M + 127) / 128;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    uint8_t* p = base ? base + off : nullptr;
+    off = align_up(off + bytes, 256);
+    return p;
+  };
+  Workspace t;
+  t.lengths = reinterpret_cast<int*>(take(sizeof(int) * B));
+  t.general = take(B);
+  t.tile_list = reinterpret_cast<int*>(take(sizeof(int) * tiles));
+  t.n_live = reinterpret_cast<int*>(take(sizeof(int)));
+  t.tile_live = take(tiles);
+  t.act = reinterpret_cast<__half*>(take(2 * M * c.d_model));
+  t.q = reinterpret_cast<__half*>(take(2 * M * c.d_model));
+  t.k = reinterpret_cast<__half*>(take(2 * M * c.d_model));
+  t.v = reinterpret_cast<__half*>(take(2 * M * c.d_model));
+  t.ff = reinterpret_cast<__half*>(take(2 * M * c.ffn_dim));
+  if (w) *w = t;
+  return off;
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------ model object
+struct TjLayerPacked {
+  __half* wqkv;  // [3d, d]
+  __half* wo;    // [d, d]
+  __half* w1;    // [F, d]
+  __half* w2;    // [d, F]
+  float* bqkv;   // [3d]
+  float* bo;
+  float* b1;
+  float* b2;
+  float* ln1_g;
+  float* ln1_b;
+  float* ln2_g;
+  float* ln2_b;
+};
+
+struct TjModel {
+  TjConfig cfg;
+  int device;
+  std::vector<TjLayerPacked> layers;
+  float* final_g = nullptr;
+  float* final_b = nullptr;
+  void* weights = nullptr;  // single allocation for all packed parameters
+  int* err = nullptr;       // device error word
+  long long launches = 0;   // kernels launched through this model
+  // per-launch event profiling (tj_profile_begin / tj_profile_end)
+  bool prof_on = false;
+  int prof_max = 0;
+  int prof_n = 0;
+  std::vector<cudaEvent_t> prof_ev;  // 2 per launch
+  std::vector<int> prof_cls;
+};
+
+namespace {
+// Runs one launcher, counting its kernels and bracketing it with an event pair
+// when profiling is active.
+template <class F>
+int timed_launch(TjModel* m, int cls, int kernels, cudaStream_t st, F&& launch) {
+  const bool rec = m->prof_on && m->prof_n < m->prof_max;
+  if (rec) TJ_CUDA(cudaEventRecord(m->prof_ev[2 * m->prof_n], st));
+  const int s = launch();
+  if (s != TJ_OK) return s;
+  m->launches += kernels;
+  if (rec) {
+    TJ_CUDA(cudaEventRecord(m->prof_ev[2 * m->prof_n + 1], st));
+    m->prof_cls[m->prof_n] = cls;
+    ++m->prof_n;
+  }
+  return TJ_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int tj_version(void) { return 1; }
+
+const char* tj_last_error(void) { return g_last_error.c_str(); }
+
+int tj_model_create(const TjConfig* cfg, TjModel** out) {
+  if (!cfg || !out) return fail(TJ_ERR_INVALID, "null argument");
+  *out = nullptr;
+  const TjConfig c = *cfg;
+  if (c.d_model <= 0 || c.num_heads <= 0 || c.ffn_dim <= 0 || c.num_layers <= 0)
+    return fail(TJ_ERR_INVALID, "config fields must be positive");
+  if (c.d_model % c.num_heads) return fail(TJ_ERR_INVALID, "d_model %% num_heads != 0");
+  const int hd = c.d_model / c.num_heads;
+  if (hd != 32 && hd != 64 && hd != 128) return fail(TJ_ERR_UNSUPPORTED, "head_dim %d not supported (32, 64, 128)", hd);
+  if (c.d_model % 64 || c.ffn_dim % 64) return fail(TJ_ERR_UNSUPPORTED, "d_model and ffn_dim must be multiples of 64");
+  if (c.d_model > 4096) return fail(TJ_ERR_UNSUPPORTED, "d_model > 4096");
+  DeviceInfo di;
+  TJ_CHECK(device_info(&di));
+  TjModel* m = new TjModel();
+  m->cfg = c;
+  if (m->cfg.layer_norm_eps <= 0.f) m->cfg.layer_norm_eps = 1e-5f;
+  TJ_CUDA(cudaGetDevice(&m->device));
+  const size_t d = c.d_model, F = c.ffn_dim;
+  const size_t per_layer = align_up(2 * 3 * d * d, 256) + align_up(2 * d * d, 256) + align_up(2 * F * d, 256) +
+                           align_up(2 * d * F, 256) + align_up(4 * 3 * d, 256) + 3 * align_up(4 * d, 256) +
+                           align_up(4 * F, 256) + 4 * align_up(4 * d, 256);
+  const size_t total = per_layer * c.num_layers + 2 * align_up(4 * d, 256) + 256;
+  cudaError_t e = cudaMalloc(&m->weights, total);
+  if (e != cudaSuccess) { delete m; return fail(TJ_ERR_CUDA, "cudaMalloc weights: %s", cudaGetErrorString(e)); }
+  e = cudaMalloc(&m->err, sizeof(int));
+  if (e != cudaSuccess) { cudaFree(m->weights); delete m; return fail(TJ_ERR_CUDA, "cudaMalloc err: %s", cudaGetErrorString(e)); }
+  cudaMemset(m->err, 0, sizeof(int));
+  uint8_t* p = static_cast<uint8_t*>(m->weights);
+  auto take = [&](size_t bytes) { uint8_t* r = p; p += align_up(bytes, 256); return r; };
+  m->layers.resize(c.num_layers);
+  for (auto& L : m->layers) {
+    L.wqkv = reinterpret_cast<__half*>(take(2 * 3 * d * d));
+    L.wo = reinterpret_cast<__half*>(take(2 * d * d));
+    L.w1 = reinterpret_cast<__half*>(take(2 * F * d));
+    L.w2 = reinterpret_cast<__half*>(take(2 * d * F));
+    L.bqkv = reinterpret_cast<float*>(take(4 * 3 * d));
+    L.bo = reinterpret_cast<float*>(take(4 * d));
+    L.b2 = reinterpret_cast<float*>(take(4 * d));
+    L.ln1_g = reinterpret_cast<float*>(take(4 * d));
+    L.b1 = reinterpret_cast<float*>(take(4 * F));
+    L.ln1_b = reinterpret_cast<float*>(take(4 * d));
+    L.ln2_g = reinterpret_cast<float*>(take(4 * d));
+    L.ln2_b = reinterpret_cast<float*>(take(4 * d));
+  }
+  m->final_g = reinterpret_cast<float*>(take(4 * d));
+  m->final_b = reinterpret_cast<float*>(take(4 * d));
+  *out = m;
+  return TJ_OK;
+}
+
+int tj_model_destroy(TjModel* m) {
+  if (!m) return TJ_OK;
+  for (cudaEvent_t e : m->prof_ev) cudaEventDestroy(e);
+  cudaFree(m->weights);
+  cudaFree(m->err);
+  delete m;
+  return TJ_OK;
+}
+
+static int convert(const float* src, __half* dst, size_t n, cudaStream_t st) {
+  const int blocks = (int)std::min<size_t>((n + 255) / 256, 4096);
+  tj::f32_to_f16_kernel<<<blocks, 256, 0, st>>>(src, dst, (long long)n);
+  TJ_CUDA(cudaGetLastError());
+  return TJ_OK;
+}
+
+int tj_model_load_layer(TjModel* m, int layer, const TjLayerParams* P, void* stream) {
+  if (!m || !P) return fail(TJ_ERR_INVALID, "null argument");
+  if (layer < 0 || layer >= m->cfg.num_layers) return fail(TJ_ERR_INVALID, "layer %d out of range", layer);
+  const void* ptrs[] = {P->norm1_weight, P->norm1_bias, P->q_weight, P->q_bias, P->k_weight, P->k_bias,
+                        P->v_weight, P->v_bias, P->out_weight, P->out_bias, P->norm2_weight, P->norm2_bias,
+                        P->ffn_in_weight, P->ffn_in_bias, P->ffn_out_weight, P->ffn_out_bias};
+  for (const void* q : ptrs)
+    if (!q) return fail(TJ_ERR_INVALID, "null parameter pointer");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const size_t d = m->cfg.d_model, F = m->cfg.ffn_dim;
+  TjLayerPacked& L = m->layers[layer];
+  TJ_CHECK(convert(P->q_weight, L.wqkv, d * d, st));
+  TJ_CHECK(convert(P->k_weight, L.wqkv + d * d, d * d, st));
+  TJ_CHECK(convert(P->v_weight, L.wqkv + 2 * d * d, d * d, st));
+  TJ_CHECK(convert(P->out_weight, L.wo, d * d, st));
+  TJ_CHECK(convert(P->ffn_in_weight, L.w1, F * d, st));
+  TJ_CHECK(convert(P->ffn_out_weight, L.w2, d * F, st));
+  TJ_CUDA(cudaMemcpyAsync(L.bqkv, P->q_bias, 4 * d, cudaMemcpyDeviceToDevice, st));
+  TJ_CUDA(cudaMemcpyAsync(L.bqkv + d, P->k_bias, 4 * d, cudaMemcpyDeviceToDevice, st));
+  TJ_CUDA(cudaMemcpyAsync(L.bqkv + 2 * d, P->v_bias, 4 * d, cudaMemcpyDeviceToDevice, st));
+  TJ_CUDA(cudaMemcpyAsync(L.bo, P->out_bias, 4 * d, cudaMemcpyDeviceToDevice, st));
+  TJ_CUDA(cudaMemcpyAsync(L.b1, P->ffn_in_bias, 4 * F, cudaMemcpyDeviceToDevice, st));
+  TJ_CUDA(cudaMemcpyAsync(L.b2, P->ffn_out_bias, 4 * d, cudaMemcpyDeviceToDevice, st));
+  TJ_CUDA(cudaMemcpyAsync(L.ln1_g, P->norm1_weight, 4 * d, cudaMemcpyDeviceToDevice, st));
+  TJ_CUDA(cudaMemcpyAsync(L.ln1_b, P->norm1_bias, 4 * d, cudaMemcpyDeviceToDevice, st));
+  TJ_CUDA(cudaMemcpyAsync(L.ln2_g, P->norm2_weight, 4 * d, cudaMemcpyDeviceToDevice, st));
+  TJ_CUDA(cudaMemcpyAsync(L.ln2_b, P->norm2_bias, 4 * d, cudaMemcpyDeviceToDevice, st));
+  return TJ_OK;
+}
+
+int tj_model_load_final_norm(TjModel* m, const float* w, const float* b, void* stream) {
+  if (!m || !w || !b) return fail(TJ_ERR_INVALID, "null argument");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  TJ_CUDA(cudaMemcpyAsync(m->final_g, w, 4 * (size_t)m->cfg.d_model, cudaMemcpyDeviceToDevice, st));
+  TJ_CUDA(cudaMemcpyAsync(m->final_b, b, 4 * (size_t)m->cfg.d_model, cudaMemcpyDeviceToDevice, st));
+  return TJ_OK;
+}
+
+int tj_workspace_bytes(const TjModel* m, int B, int S, size_t* bytes) {
+  if (!m || !bytes) return fail(TJ_ERR_INVALID, "null argument");
+  if (B < 0 || S < 0) return fail(TJ_ERR_INVALID, "negative shape");
+  *bytes = carve(m->cfg, B, S, nullptr, nullptr);
+  return TJ_OK;
+}
+
+int tj_device_error(TjModel* m, int* code) {
+  if (!m || !code) return fail(TJ_ERR_INVALID, "null argument");
+  TJ_CUDA(cudaMemcpy(code, m->err, sizeof(int), cudaMemcpyDeviceToHost));
+  TJ_CUDA(cudaMemset(m->err, 0, sizeof(int)));
+  return TJ_OK;
+}
+
+int tj_forward(TjModel* m, const float* x, const uint8_t* mask, float* out, int B, int S, int route, void* ws,
+               size_t ws_bytes, void* stream) {
+  if (!m || !x || !out || !ws) return fail(TJ_ERR_INVALID, "null argument");
+  if (B <= 0 || S <= 0) return fail(TJ_ERR_INVALID, "batch and seq_len must be positive");
+  if (x == out) return fail(TJ_ERR_INVALID, "x and out must not alias");
+  if (route != TJ_ROUTE_EXACT && route != TJ_ROUTE_AUTO)
+    return fail(TJ_ERR_UNSUPPORTED, "attention route %d not available in this build", route);
+  const TjConfig& c = m->cfg;
+  const size_t need = carve(c, B, S, nullptr, nullptr);
+  if (ws_bytes < need) return fail(TJ_ERR_INVALID, "workspace %zu bytes < required %zu", ws_bytes, need);
+  if ((reinterpret_cast<uintptr_t>(ws) & 255) != 0) return fail(TJ_ERR_INVALID, "workspace not 256-byte aligned");
+  if ((long long)B * S > (1LL << 31) / 128) return fail(TJ_ERR_UNSUPPORTED, "batch*seq_len too large");
+  DeviceInfo di;
+  TJ_CHECK(device_info(&di));
+  int dev = 0;
+  TJ_CUDA(cudaGetDevice(&dev));
+  if (dev != m->device) return fail(TJ_ERR_INVALID, "model lives on device %d, current device is %d", m->device, dev);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Workspace w;
+  carve(c, B, S, static_cast<uint8_t*>(ws), &w);
+  const int d = c.d_model, H = c.num_heads, hd = d / H, F = c.ffn_dim;
+  const int M = B * S;
+
+  TJ_CHECK(timed_launch(m, TJ_K_PREP, 2, st, [&] {
+    return launch_prepare(mask, B, S, w.lengths, w.general, w.tile_list, w.n_live, w.tile_live, st);
+  }));
+  tj::RowValidity rv{w.lengths, mask, S, (long long)M};
+
+  tj::GemmParams gp{};
+  gp.M = M;
+  gp.seq = S;
+  gp.lengths = w.lengths;
+  gp.mask = mask;
+  gp.tile_list = w.tile_list;
+  gp.n_live = w.n_live;
+  gp.q = w.q; gp.k = w.k; gp.v = w.v;
+  gp.heads = H; gp.head_dim = hd; gp.d_model = d;
+  gp.err = m->err;
+
+  tj::AttnParams ap{};
+  ap.lengths = w.lengths;
+  ap.mask = mask;
+  ap.general = w.general;
+  ap.ctx = w.act;
+  ap.S = S; ap.H = H; ap.d_model = d;
+  ap.causal = c.causal ? 1 : 0;
+  ap.scale_log2 = (float)(1.0 / std::sqrt((double)hd) * 1.4426950408889634);
+  ap.err = m->err;
+
+  const float eps = c.layer_norm_eps;
+  const float* resid_in = x;
+  for (int l = 0; l < c.num_layers; ++l) {
+    const TjLayerPacked& L = m->layers[l];
+    // LN1 -> act (fp16)
+    TJ_CHECK(timed_launch(m, TJ_K_LN, 1, st, [&] {
+      return launch_layernorm(resid_in, L.ln1_g, L.ln1_b, w.act, true, false, d, eps, rv, w.tile_live, st);
+    }));
+    // packed QKV projection -> Q, K, V [B, H, S, hd]
+    gp.N = 3 * d; gp.K = d; gp.bias = L.bqkv;
+    TJ_CHECK(timed_launch(m, TJ_K_QKV, 1, st, [&] { return launch_gemm_epi(tj::kEpiQKV, w.act, L.wqkv, gp, di.sms, st); }));
+    // attention -> ctx (reuses act)
+    TJ_CHECK(timed_launch(m, TJ_K_ATTN, 1, st, [&] { return launch_attention(w.q, w.k, w.v, hd, ap, B, st); }));
+    // out projection + residual -> out (fp32 residual stream)
+    gp.N = d; gp.K = d; gp.bias = L.bo; gp.out32 = out; gp.resid = resid_in;
+    TJ_CHECK(timed_launch(m, TJ_K_OUT, 1, st, [&] { return launch_gemm_epi(tj::kEpiResid, w.act, L.wo, gp, di.sms, st); }));
+    // LN2 -> act
+    TJ_CHECK(timed_launch(m, TJ_K_LN, 1, st, [&] {
+      return launch_layernorm(out, L.ln2_g, L.ln2_b, w.act, true, false, d, eps, rv, w.tile_live, st);
+    }));
+    // FFN in + GELU -> ff
+    gp.N = F; gp.K = d; gp.bias = L.b1; gp.out16 = w.ff;
+    TJ_CHECK(timed_launch(m, TJ_K_FFN_IN, 1, st, [&] { return launch_gemm_epi(tj::kEpiGelu, w.act, L.w1, gp, di.sms, st); }));
+    // FFN out + residual (in place) -> out
+    gp.N = d; gp.K = F; gp.bias = L.b2; gp.out32 = out; gp.resid = out;
+    TJ_CHECK(timed_launch(m, TJ_K_FFN_OUT, 1, st, [&] { return launch_gemm_epi(tj::kEpiResid, w.ff, L.w2, gp, di.sms, st); }));
+    resid_in = out;
+  }
+  // final LayerNorm in place; every invalid row becomes exactly 0
+  TJ_CHECK(timed_launch(m, TJ_K_LN_FINAL, 1, st, [&] {
+    return launch_layernorm(out, m->final_g, m->final_b, out, false, true, d, eps, rv, w.tile_live, st);
+  }));
+  return TJ_OK;
+}
+
+int tj_profile_begin(TjModel* m, int max_launches) {
+  if (!m || max_launches <= 0) return fail(TJ_ERR_INVALID, "bad profile arguments");
+  if ((int)m->prof_cls.size() < max_launches) {
+    const size_t have = m->prof_ev.size();
+    m->prof_ev.resize(2 * (size_t)max_launches);
+    for (size_t i = have; i < m->prof_ev.size(); ++i) TJ_CUDA(cudaEventCreate(&m->prof_ev[i]));
+    m->prof_cls.resize(max_launches);
+  }
+  m->prof_max = max_launches;
+  m->prof_n = 0;
+  m->prof_on = true;
+  return TJ_OK;
+}
+
+int tj_profile_end(TjModel* m, double* ms, long long* counts) {
+  if (!m || !ms || !counts) return fail(TJ_ERR_INVALID, "null argument");
+  for (int i = 0; i < TJ_K_COUNT; ++i) { ms[i] = 0.0; counts[i] = 0; }
+  m->prof_on = false;
+  for (int i = 0; i < m->prof_n; ++i) {
+    TJ_CUDA(cudaEventSynchronize(m->prof_ev[2 * i + 1]));
+    float t = 0.f;
+    TJ_CUDA(cudaEventElapsedTime(&t, m->prof_ev[2 * i], m->prof_ev[2 * i + 1]));
+    ms[m->prof_cls[i]] += t;
+    counts[m->prof_cls[i]] += 1;
+  }
+  m->prof_n = 0;
+  return TJ_OK;
+}
+
+int tj_launch_count(TjModel* m, long long* count) {
+  if (!m || !count) return fail(TJ_ERR_INVALID, "null argument");
+  *count = m->launches;
+  return TJ_OK;
+}
+
+// ------------------------------------------------------------------ building blocks
+int tj_prepare_mask(const uint8_t* mask, int B, int S, int* lengths, uint8_t* general, int* tile_list, int* n_live,
+                    uint8_t* tile_live, void* stream) {
+  if (!lengths || !general || !tile_list || !n_live || !tile_live) return fail(TJ_ERR_INVALID, "null argument");
+  if (B <= 0 || S <= 0) return fail(TJ_ERR_INVALID, "batch and seq_len must be positive");
+  return launch_prepare(mask, B, S, lengths, general, tile_list, n_live, tile_live, static_cast<cudaStream_t>(stream));
+}
+
+int tj_layernorm(const float* x, const float* g, const float* b, int B, int S, int d, float eps, void* out,
+                 int out_fp16, const int* lengths, const uint8_t* mask, const uint8_t* tile_live, void* stream) {
+  if (!x || !g || !b || !out || !lengths || !tile_live) return fail(TJ_ERR_INVALID, "null argument");
+  tj::RowValidity rv{lengths, mask, S, (long long)B * S};
+  return launch_layernorm(x, g, b, out, out_fp16 != 0, out_fp16 == 0, d, eps, rv, tile_live,
+                          static_cast<cudaStream_t>(stream));
+}
+
+int tj_gemm_f16(const void* a, const void* wgt, const float* bias, int B, int S, int n, int k, int epilogue, void* out,
+                const float* resid, void* q, void* kk, void* v, int heads, const int* tile_list, const int* n_live,
+                const int* lengths, const uint8_t* mask, int* err, void* stream) {
+  if (!a || !wgt || !bias || !tile_list || !n_live || !lengths || !err) return fail(TJ_ERR_INVALID, "null argument");
+  if (n % 32 || k % 8) return fail(TJ_ERR_UNSUPPORTED, "need n %% 32 == 0 and k %% 8 == 0");
+  DeviceInfo di;
+  TJ_CHECK(device_info(&di));
+  tj::GemmParams p{};
+  p.M = B * S; p.N = n; p.K = k; p.seq = S;
+  p.lengths = lengths; p.mask = mask; p.tile_list = tile_list; p.n_live = n_live; p.bias = bias; p.err = err;
+  if (epilogue == TJ_EPI_QKV) {
+    if (!q || !kk || !v || heads <= 0 || n % 3 || (n / 3) % heads) return fail(TJ_ERR_INVALID, "bad QKV arguments");
+    p.q = static_cast<__half*>(q); p.k = static_cast<__half*>(kk); p.v = static_cast<__half*>(v);
+    p.heads = heads; p.d_model = n / 3; p.head_dim = p.d_model / heads;
+    if (p.head_dim % 32) return fail(TJ_ERR_UNSUPPORTED, "head_dim must be a multiple of 32");
+  } else if (epilogue == TJ_EPI_RESID) {
+    if (!out || !resid) return fail(TJ_ERR_INVALID, "null out/resid");
+    p.out32 = static_cast<float*>(out); p.resid = resid;
+  } else {
+    if (!out) return fail(TJ_ERR_INVALID, "null out");
+    p.out16 = static_cast<__half*>(out);
+  }
+  return launch_gemm_epi(epilogue, a, wgt, p, di.sms, static_cast<cudaStream_t>(stream));
+}
+
+int tj_attention_f16(const void* q, const void* k, const void* v, void* ctx, int B, int H, int S, int hd, int causal,
+                     const int* lengths, const uint8_t* mask, const uint8_t* general, int* err, void* stream) {
+  if (!q || !k || !v || !ctx || !lengths || !general || !err) return fail(TJ_ERR_INVALID, "null argument");
+  DeviceInfo di;
+  TJ_CHECK(device_info(&di));
+  tj::AttnParams p{};
+  p.lengths = lengths; p.mask = mask; p.general = general; p.ctx = static_cast<__half*>(ctx);
+  p.S = S; p.H = H; p.d_model = H * hd; p.causal = causal ? 1 : 0;
+  p.scale_log2 = (float)(1.0 / std::sqrt((double)hd) * 1.4426950408889634);
+  p.err = err;
+  return launch_attention(q, k, v, hd, p, B, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,244 @@
+// Persistent warp-specialised tcgen05 GEMM with fused epilogues.
+//
+//   C[M, N] = A[M, K] * W[N, K]^T     (A, W fp16 K-major; fp32 accumulate in TMEM)
+//
+// One CTA per SM.  Warp 0 issues TMA loads into a STAGES-deep shared-memory
+// ring, warp 1 (one thread) issues tcgen05.mma into one of two TMEM
+// accumulators, warps 2..5 drain the other accumulator through the epilogue
+// (tcgen05.ld -> bias / GELU / residual / head scatter -> global).  M tiles
+// that hold no valid token (right padding) are dropped up front: the kernel
+// walks a compact device-side list of live 128-row tiles.
+#pragma once
+#include "tj_common.cuh"
+
+namespace tj {
+
+enum EpiKind : int { kEpiQKV = 0, kEpiGelu = 1, kEpiResid = 2, kEpiPlain16 = 3 };
+
+struct GemmParams {
+  int M, N, K;
+  int seq;               // rows per sample (row -> (b, n) = (row / seq, row % seq))
+  const int* lengths;    // [B] valid-prefix length per sample
+  const uint8_t* mask;   // [B*seq] per-row validity, or null (prefix lengths only)
+  const int* tile_list;  // live 128-row tile indices
+  const int* n_live;     // number of entries in tile_list
+  const float* bias;     // [N]
+  // kEpiQKV: Q,K,V as [B, H, seq, hd] fp16
+  __half* q;
+  __half* k;
+  __half* v;
+  int heads, head_dim, d_model;
+  // kEpiGelu / kEpiPlain16: out16 [M, N]
+  __half* out16;
+  // kEpiResid: out32[row, :] = resid[row, :] + acc + bias (resid may alias out32)
+  float* out32;
+  const float* resid;
+  int* err;
+};
+
+constexpr int kGemmBM = 128;
+constexpr int kGemmBK = 64;  // one 128-byte swizzle atom of fp16
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int kStageA = kGemmBM * kGemmBK * 2;
+  static constexpr int kStageB = BN * kGemmBK * 2;
+  static constexpr int kStageBytes = kStageA + kStageB;
+  static constexpr int kStages = (200 * 1024) / kStageBytes;
+  static constexpr int kTmemCols = 2 * BN;  // double-buffered accumulator
+  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int kThreads = 192;
+};
+
+TJ_DEV bool row_is_valid(const GemmParams& p, int row) {
+  if (row >= p.M) return false;
+  const int b = row / p.seq;
+  const int n = row - b * p.seq;
+  if (n >= __ldg(p.lengths + b)) return false;
+  return p.mask == nullptr || __ldg(p.mask + row) != 0;
+}
+
+TJ_DEV float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752440f)); }
+
+template <int EPI>
+TJ_DEV void epilogue_chunk(const GemmParams& p, int row, bool valid, int col0, const uint32_t (&acc)[32]) {
+  float v[32];
+  if (valid) {
+#pragma unroll
+    for (int j = 0; j < 32; j += 4) {
+      const float4 bb = __ldg(reinterpret_cast<const float4*>(p.bias + col0 + j));
+      v[j] = __uint_as_float(acc[j]) + bb.x;
+      v[j + 1] = __uint_as_float(acc[j + 1]) + bb.y;
+      v[j + 2] = __uint_as_float(acc[j + 2]) + bb.z;
+      v[j + 3] = __uint_as_float(acc[j + 3]) + bb.w;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = 0.0f;
+  }
+  if constexpr (EPI == kEpiResid) {
+    float* dst = p.out32 + (size_t)row * p.N + col0;
+    if (valid) {
+      const float* src = p.resid + (size_t)row * p.N + col0;
+#pragma unroll
+      for (int j = 0; j < 32; j += 4) {
+        const float4 r = *reinterpret_cast<const float4*>(src + j);
+        v[j] += r.x; v[j + 1] += r.y; v[j + 2] += r.z; v[j + 3] += r.w;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 32; j += 4)
+      *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+  } else {
+    if constexpr (EPI == kEpiGelu) {
+      if (valid) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = gelu_erf(v[j]);
+      }
+    }
+    __half* dst;
+    if constexpr (EPI == kEpiQKV) {
+      const int which = col0 / p.d_model;
+      const int hc = col0 - which * p.d_model;
+      const int head = hc / p.head_dim;
+      const int dim0 = hc - head * p.head_dim;
+      const int b = row / p.seq;
+      const int n = row - b * p.seq;
+      __half* base = which == 0 ? p.q : (which == 1 ? p.k : p.v);
+      dst = base + (((size_t)b * p.heads + head) * p.seq + n) * p.head_dim + dim0;
+    } else {
+      dst = p.out16 + (size_t)row * p.N + col0;
+    }
+#pragma unroll
+    for (int j = 0; j < 32; j += 8) {
+      uint4 w;
+      w.x = pack_half2(v[j], v[j + 1]);
+      w.y = pack_half2(v[j + 2], v[j + 3]);
+      w.z = pack_half2(v[j + 4], v[j + 5]);
+      w.w = pack_half2(v[j + 6], v[j + 7]);
+      *reinterpret_cast<uint4*>(dst + j) = w;
+    }
+  }
+}
+
+template <int BN, int EPI>
+__global__ void __launch_bounds__(192, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
+                   const GemmParams p) {
+  using Cfg = GemmCfg<BN>;
+  constexpr int S = Cfg::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes);
+  uint64_t* full = bars;             // [S]
+  uint64_t* empty = bars + S;        // [S]
+  uint64_t* acc_full = bars + 2 * S; // [2]
+  uint64_t* acc_empty = acc_full + 2;// [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) { mbar_init(full + i, 1); mbar_init(empty + i, 1); }
+    for (int i = 0; i < 2; ++i) { mbar_init(acc_full + i, 1); mbar_init(acc_empty + i, 128); }
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, Cfg::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int n_tiles = (p.N + BN - 1) / BN;
+  const int total = __ldg(p.n_live) * n_tiles;
+  const int k_blocks = (p.K + kGemmBK - 1) / kGemmBK;
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------------------------------------ TMA producer
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmW);
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+      const int mt = __ldg(p.tile_list + t / n_tiles);
+      const int nt = t % n_tiles;
+      for (int kb = 0; kb < k_blocks; ++kb) {
+        if (!mbar_wait(empty + stage, phase ^ 1u, p.err, kErrGemmProducer)) { ok = false; break; }
+        uint8_t* sa = smem + stage * Cfg::kStageBytes;
+        uint8_t* sb = sa + Cfg::kStageA;
+        mbar_expect_tx(full + stage, Cfg::kStageBytes);
+        tma_load_2d(sa, &tmA, full + stage, kb * kGemmBK, mt * kGemmBM);
+        tma_load_2d(sb, &tmW, full + stage, kb * kGemmBK, nt * BN);
+        if (++stage == S) { stage = 0; phase ^= 1u; }
+      }
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ------------------------------------------------------------ MMA issuer
+    constexpr uint32_t idesc = idesc_f16_f32(kGemmBM, BN, false, false);
+    int stage = 0;
+    uint32_t phase = 0;
+    int abuf = 0;
+    uint32_t aphase = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+      if (!mbar_wait(acc_empty + abuf, aphase ^ 1u, p.err, kErrGemmMma)) break;
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + abuf * BN;
+      for (int kb = 0; kb < k_blocks; ++kb) {
+        if (!mbar_wait(full + stage, phase, p.err, kErrGemmMma)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t sa = smem_u32(smem + stage * Cfg::kStageBytes);
+        const uint32_t sb = sa + Cfg::kStageA;
+#pragma unroll
+        for (int ks = 0; ks < kGemmBK / 16; ++ks) {
+          const uint64_t ad = smem_desc(sa + ks * 32, 16, 1024, 128);
+          const uint64_t bd = smem_desc(sb + ks * 32, 16, 1024, 128);
+          umma_f16_ss(d_tmem, ad, bd, idesc, (kb | ks) != 0);
+        }
+        umma_commit(empty + stage);  // release the smem stage when these MMAs retire
+        if (++stage == S) { stage = 0; phase ^= 1u; }
+      }
+      if (!ok) break;
+      umma_commit(acc_full + abuf);
+      if (++abuf == 2) { abuf = 0; aphase ^= 1u; }
+    }
+  } else if (warp >= 2) {
+    // ------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    const int row_in_tile = quarter * 32 + lane;
+    int abuf = 0;
+    uint32_t aphase = 0;
+    for (int t = blockIdx.x; t < total; t += gridDim.x) {
+      const int mt = __ldg(p.tile_list + t / n_tiles);
+      const int nt = t % n_tiles;
+      if (!mbar_wait(acc_full + abuf, aphase, p.err, kErrGemmEpilogue)) break;
+      tc_fence_after();
+      const int row = mt * kGemmBM + row_in_tile;
+      const bool in_range = row < p.M;
+      const bool valid = row_is_valid(p, row);
+      const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + abuf * BN;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t acc[32];
+        tmem_ld32(taddr + c * 32, acc);
+        tmem_ld_wait();
+        const int col0 = nt * BN + c * 32;
+        if (in_range && col0 < p.N) epilogue_chunk<EPI>(p, row, valid, col0, acc);
+      }
+      tc_fence_before();
+      mbar_arrive(acc_empty + abuf);
+      if (++abuf == 2) { abuf = 0; aphase ^= 1u; }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem_base, Cfg::kTmemCols);
+}
+
+}  // namespace tj

@@ -1,0 +1,184 @@
+// Memory-bound helper kernels: mask -> lengths / live-tile list, LayerNorm,
+// and the one-time weight packing (fp32 nn.Linear weights -> fp16).
+#pragma once
+#include "tj_common.cuh"
+
+namespace tj {
+
+constexpr int kTileRows = 128;
+
+// Per sample: length = 1 + last valid position (0 if none); general = mask is
+// not a right-padded prefix.  mask == null means every position is valid.
+__global__ void prep_lengths_kernel(const uint8_t* __restrict__ mask, int S, int* __restrict__ lengths,
+                                    uint8_t* __restrict__ general) {
+  const int b = blockIdx.x;
+  if (mask == nullptr) {
+    if (threadIdx.x == 0) { lengths[b] = S; general[b] = 0; }
+    return;
+  }
+  const uint8_t* m = mask + (size_t)b * S;
+  int last = 0, count = 0;
+  for (int i = threadIdx.x; i < S; i += blockDim.x) {
+    if (m[i]) { last = i + 1; ++count; }
+  }
+  __shared__ int s_last[32], s_count[32];
+  for (int o = 16; o > 0; o >>= 1) {
+    last = max(last, __shfl_xor_sync(0xffffffffu, last, o));
+    count += __shfl_xor_sync(0xffffffffu, count, o);
+  }
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  if (l == 0) { s_last[w] = last; s_count[w] = count; }
+  __syncthreads();
+  if (w == 0) {
+    const int nw = blockDim.x >> 5;
+    last = l < nw ? s_last[l] : 0;
+    count = l < nw ? s_count[l] : 0;
+    for (int o = 16; o > 0; o >>= 1) {
+      last = max(last, __shfl_xor_sync(0xffffffffu, last, o));
+      count += __shfl_xor_sync(0xffffffffu, count, o);
+    }
+    if (l == 0) { lengths[b] = last; general[b] = (count != last) ? 1 : 0; }
+  }
+}
+
+// Compact list of 128-row tiles (over the flattened [B*S] rows) holding at
+// least one row inside its sample's valid prefix.  One block of 1024 threads.
+__global__ void prep_tiles_kernel(const int* __restrict__ lengths, int B, int S, int* __restrict__ tile_list,
+                                  int* __restrict__ n_live, uint8_t* __restrict__ tile_live) {
+  const long long M = (long long)B * S;
+  const int n_tiles = (int)((M + kTileRows - 1) / kTileRows);
+  __shared__ int s_warp[32];
+  __shared__ int s_base;
+  if (threadIdx.x == 0) s_base = 0;
+  __syncthreads();
+  for (int start = 0; start < n_tiles; start += blockDim.x) {
+    const int t = start + threadIdx.x;
+    int live = 0;
+    if (t < n_tiles) {
+      const long long r0 = (long long)t * kTileRows;
+      const long long r1 = min(r0 + kTileRows, M) - 1;
+      for (long long b = r0 / S; b <= r1 / S; ++b) {
+        const long long first = max(r0, b * S) - b * S;
+        if (first < lengths[b]) { live = 1; break; }
+      }
+      tile_live[t] = (uint8_t)live;
+    }
+    // block-wide exclusive scan of `live`
+    const int l = threadIdx.x & 31, w = threadIdx.x >> 5;
+    int incl = live;
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (l >= o) incl += v;
+    }
+    if (l == 31) s_warp[w] = incl;
+    __syncthreads();
+    if (w == 0) {
+      int v = s_warp[l];
+      for (int o = 1; o < 32; o <<= 1) {
+        const int u = __shfl_up_sync(0xffffffffu, v, o);
+        if (l >= o) v += u;
+      }
+      s_warp[l] = v;
+    }
+    __syncthreads();
+    const int excl = incl - live + (w > 0 ? s_warp[w - 1] : 0);
+    if (live) tile_list[s_base + excl] = t;
+    __syncthreads();
+    if (threadIdx.x == blockDim.x - 1) s_base += excl + live;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) *n_live = s_base;
+}
+
+struct RowValidity {
+  const int* lengths;
+  const uint8_t* mask;
+  int S;
+  long long M;
+  __device__ bool operator()(long long row) const {
+    if (row >= M) return false;
+    const int b = (int)(row / S);
+    const int n = (int)(row - (long long)b * S);
+    if (n >= __ldg(lengths + b)) return false;
+    return mask == nullptr || __ldg(mask + row) != 0;
+  }
+};
+
+// One warp per row, d <= 32*4*VPL.  Valid rows: (x-mean)/sqrt(var+eps)*g+b.
+// Invalid rows inside live tiles (or every invalid row when ALL_ROWS) are
+// written as zeros; rows of dead tiles are skipped.
+template <int VPL, bool OUT_F16, bool ALL_ROWS>
+__global__ void __launch_bounds__(256) layernorm_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
+                                                        const float* __restrict__ beta, void* __restrict__ out,
+                                                        int d, float eps, RowValidity valid,
+                                                        const uint8_t* __restrict__ tile_live) {
+  const long long row = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= valid.M) return;
+  const bool ok = valid(row);
+  if (!ok && !ALL_ROWS && tile_live[row / kTileRows] == 0) return;
+  const int nvec = d >> 2;
+  float4 v[VPL];
+  if (ok) {
+    const float4* src = reinterpret_cast<const float4*>(x + row * d);
+    float sum = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      const int c = lane + 32 * i;
+      v[i] = c < nvec ? src[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+      sum += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    const float mean = sum / d;
+    float sq = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      const int c = lane + 32 * i;
+      if (c < nvec) {
+        const float a = v[i].x - mean, bb = v[i].y - mean, cc = v[i].z - mean, dd = v[i].w - mean;
+        sq += (a * a + bb * bb) + (cc * cc + dd * dd);
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+    const float rstd = rsqrtf(sq / d + eps);
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      const int c = lane + 32 * i;
+      if (c < nvec) {
+        const float4 g = __ldg(reinterpret_cast<const float4*>(gamma) + c);
+        const float4 bt = __ldg(reinterpret_cast<const float4*>(beta) + c);
+        v[i].x = (v[i].x - mean) * rstd * g.x + bt.x;
+        v[i].y = (v[i].y - mean) * rstd * g.y + bt.y;
+        v[i].z = (v[i].z - mean) * rstd * g.z + bt.z;
+        v[i].w = (v[i].w - mean) * rstd * g.w + bt.w;
+      }
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int c = lane + 32 * i;
+    if (c < nvec) {
+      if constexpr (OUT_F16) {
+        uint2 w;
+        w.x = pack_half2(v[i].x, v[i].y);
+        w.y = pack_half2(v[i].z, v[i].w);
+        reinterpret_cast<uint2*>(static_cast<__half*>(out) + row * d)[c] = w;
+      } else {
+        reinterpret_cast<float4*>(static_cast<float*>(out) + row * d)[c] = v[i];
+      }
+    }
+  }
+}
+
+// dst = fp16(src), element-wise, for the packed weight buffers.
+__global__ void f32_to_f16_kernel(const float* __restrict__ src, __half* __restrict__ dst, long long n) {
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+    dst[i] = __float2half_rn(src[i]);
+}
+
+}  // namespace tj

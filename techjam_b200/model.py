@@ -1,0 +1,218 @@
+"""Reference-compatible ``nn.Module`` whose forward runs entirely in ``libtj.so``.
+
+``B200Transformer(config)`` has exactly the parameter tree of the reference's
+``BaselineTransformer`` (torch_transformer_benchmark.py:59-172): ``layers.{i}
+.norm1/.attention.{q,k,v,out}_proj/.norm2/.ffn_in/.ffn_out`` and
+``final_norm``, created in the same order, so ``copy_model_weights`` (a strict
+``load_state_dict``, :203-213) works unchanged and seeded construction draws
+the same weights.  The parameters stay the single source of truth; the C
+library keeps packed FP16 copies that are rebuilt whenever a parameter's
+storage or version changes (the reference's packed-QKV rebuild hook,
+src/implementations/sdpa.py:96-124, serves the same purpose).
+
+``forward(x, valid_token_mask)`` follows the reference's signature and
+semantics (:162-172): FP32 ``[B, N, d]`` in, ``[B, N, d]`` out, padded rows
+exactly 0.  It only accepts CUDA tensors on an sm_100 device: there is no CPU
+path.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import weakref
+from typing import Dict, Optional, Tuple
+
+import torch
+import torch.nn as nn
+
+from . import _lib
+
+
+class Attention(nn.Module):
+    """Parameter container mirroring ``BaselineSelfAttention`` (:59-83)."""
+
+    def __init__(self, d_model: int, num_heads: int) -> None:
+        super().__init__()
+        if d_model % num_heads != 0:
+            raise ValueError("d_model must be divisible by num_heads")
+        self.d_model = d_model
+        self.num_heads = num_heads
+        self.head_dim = d_model // num_heads
+        self.scale = self.head_dim ** -0.5
+        self.q_proj = nn.Linear(d_model, d_model, bias=True)
+        self.k_proj = nn.Linear(d_model, d_model, bias=True)
+        self.v_proj = nn.Linear(d_model, d_model, bias=True)
+        self.out_proj = nn.Linear(d_model, d_model, bias=True)
+
+
+class Block(nn.Module):
+    """Parameter container mirroring ``BaselineTransformerBlock`` (:125-132)."""
+
+    def __init__(self, d_model: int, num_heads: int, ffn_dim: int) -> None:
+        super().__init__()
+        self.norm1 = nn.LayerNorm(d_model)
+        self.attention = Attention(d_model, num_heads)
+        self.norm2 = nn.LayerNorm(d_model)
+        self.ffn_in = nn.Linear(d_model, ffn_dim)
+        self.ffn_out = nn.Linear(ffn_dim, d_model)
+
+
+_ROUTES = {"exact": _lib.ROUTE_EXACT, "poly": _lib.ROUTE_POLY, "auto": _lib.ROUTE_AUTO}
+
+
+class _Handle:
+    """Owns one ``TjModel*`` on one device; destroyed with its Python owner."""
+
+    def __init__(self, cfg: _lib.TjConfig, device: torch.device) -> None:
+        self.device = device
+        ptr = ctypes.c_void_p()
+        with torch.cuda.device(device):
+            _lib.call("tj_model_create", ctypes.byref(cfg), ctypes.byref(ptr))
+        self.ptr = ptr
+        self._finalizer = weakref.finalize(self, _Handle._destroy, ptr)
+
+    @staticmethod
+    def _destroy(ptr) -> None:
+        try:
+            _lib.load().tj_model_destroy(ptr)
+        except Exception:  # interpreter shutdown
+            pass
+
+
+class B200Transformer(nn.Module):
+    """Drop-in replacement for the reference ``BaselineTransformer`` forward."""
+
+    def __init__(self, config, attention_route: str = "auto") -> None:
+        super().__init__()
+        if hasattr(config, "validate"):
+            config.validate()
+        self.config = config
+        self.layers = nn.ModuleList(
+            Block(config.d_model, config.num_heads, config.ffn_dim) for _ in range(config.num_layers))
+        self.final_norm = nn.LayerNorm(config.d_model)
+        if attention_route not in _ROUTES:
+            raise ValueError(f"attention_route must be one of {sorted(_ROUTES)}")
+        self.attention_route = attention_route
+        self._handle: Optional[_Handle] = None
+        self._packed_sig: Optional[Tuple] = None
+        self._workspaces: Dict[Tuple, torch.Tensor] = {}
+
+    # ---------------------------------------------------------------- packing
+    def _param_signature(self, device: torch.device) -> Tuple:
+        return (device,) + tuple((p.data_ptr(), p._version, p.dtype) for p in self.parameters())
+
+    def _tj_config(self) -> _lib.TjConfig:
+        c = self.config
+        eps = float(self.final_norm.eps)
+        return _lib.TjConfig(c.d_model, c.num_heads, c.ffn_dim, c.num_layers, int(bool(c.causal)), eps)
+
+    def _ensure_packed(self, device: torch.device) -> _Handle:
+        sig = self._param_signature(device)
+        if self._handle is not None and self._packed_sig == sig:
+            return self._handle
+        if self._handle is None or self._handle.device != device:
+            self._handle = _Handle(self._tj_config(), device)
+        stream = torch.cuda.current_stream(device)
+        keep = []
+
+        def f32(t: torch.Tensor) -> int:
+            if t.device != device:
+                raise RuntimeError(f"parameter on {t.device}, input on {device}")
+            t = t.detach()
+            if t.dtype != torch.float32 or not t.is_contiguous():
+                t = t.float().contiguous()
+            keep.append(t)
+            return t.data_ptr()
+
+        with torch.cuda.device(device):
+            for i, blk in enumerate(self.layers):
+                att = blk.attention
+                lp = _lib.TjLayerParams(
+                    f32(blk.norm1.weight), f32(blk.norm1.bias),
+                    f32(att.q_proj.weight), f32(att.q_proj.bias), f32(att.k_proj.weight), f32(att.k_proj.bias),
+                    f32(att.v_proj.weight), f32(att.v_proj.bias), f32(att.out_proj.weight), f32(att.out_proj.bias),
+                    f32(blk.norm2.weight), f32(blk.norm2.bias), f32(blk.ffn_in.weight), f32(blk.ffn_in.bias),
+                    f32(blk.ffn_out.weight), f32(blk.ffn_out.bias))
+                _lib.call("tj_model_load_layer", self._handle.ptr, i, ctypes.byref(lp),
+                          ctypes.c_void_p(stream.cuda_stream))
+            _lib.call("tj_model_load_final_norm", self._handle.ptr, f32(self.final_norm.weight),
+                      f32(self.final_norm.bias), ctypes.c_void_p(stream.cuda_stream))
+            if keep:  # temporaries must outlive the asynchronous conversion kernels
+                stream.synchronize()
+        self._packed_sig = sig
+        return self._handle
+
+    def _workspace(self, handle: _Handle, batch: int, seq_len: int, device: torch.device) -> torch.Tensor:
+        key = (device, batch, seq_len)
+        ws = self._workspaces.get(key)
+        if ws is None:
+            nbytes = ctypes.c_size_t()
+            _lib.call("tj_workspace_bytes", handle.ptr, batch, seq_len, ctypes.byref(nbytes))
+            # zero-filled once: the library only ever writes finite values into it
+            ws = torch.zeros(max(int(nbytes.value), 256), dtype=torch.uint8, device=device)
+            while len(self._workspaces) >= 4:  # keep the most recent shapes only
+                self._workspaces.pop(next(iter(self._workspaces)))
+            self._workspaces[key] = ws
+        return ws
+
+    def _apply(self, fn, recurse: bool = True):
+        # .to()/.cuda()/.half() move or replace parameters: packed copies and
+        # workspaces are rebuilt lazily at the next forward.
+        result = super()._apply(fn, recurse=recurse)
+        if hasattr(self, "_workspaces"):
+            self._packed_sig = None
+            self._workspaces = {}
+        return result
+
+    # ---------------------------------------------------------------- forward
+    def forward(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
+        if x.device.type != "cuda":
+            raise RuntimeError("techjam_b200 runs only on a CUDA sm_100 device (there is no CPU path)")
+        if x.ndim != 3 or x.shape[-1] != self.config.d_model:
+            raise ValueError(f"x must be [B, N, {self.config.d_model}], got {tuple(x.shape)}")
+        batch, seq_len, _ = x.shape
+        device = x.device
+        in_dtype = x.dtype
+        xf = x if (x.dtype == torch.float32 and x.is_contiguous()) else x.float().contiguous()
+        mask_ptr = None
+        if valid_token_mask is not None:
+            if valid_token_mask.shape != (batch, seq_len):
+                raise ValueError("valid_token_mask must be [B, N]")
+            if valid_token_mask.device != device:
+                raise ValueError("valid_token_mask must be on the input's device")
+            m = valid_token_mask
+            if m.dtype != torch.bool:
+                m = m != 0
+            m = m.contiguous()
+            mask_ptr = m.data_ptr()
+        handle = self._ensure_packed(device)
+        ws = self._workspace(handle, batch, seq_len, device)
+        out = torch.empty((batch, seq_len, self.config.d_model), dtype=torch.float32, device=device)
+        stream = torch.cuda.current_stream(device)
+        with torch.cuda.device(device):
+            _lib.call("tj_forward", handle.ptr, xf.data_ptr(), mask_ptr, out.data_ptr(), batch, seq_len,
+                      _ROUTES[self.attention_route], ws.data_ptr(), ws.numel(),
+                      ctypes.c_void_p(stream.cuda_stream))
+        return out if in_dtype == torch.float32 else out.to(in_dtype)
+
+    def device_error(self) -> int:
+        """Synchronously read and clear the device error word (0 = no expired wait)."""
+        if self._handle is None:
+            return 0
+        code = ctypes.c_int()
+        with torch.cuda.device(self._handle.device):
+            _lib.call("tj_device_error", self._handle.ptr, ctypes.byref(code))
+        return int(code.value)
+
+
+def algorithmic_flops(config, lengths) -> Tuple[float, float]:
+    """(GEMM, exact-attention) flops over valid tokens: L*2*T_v*(4d^2+2dF) and
+    L*2*d*sum l(l+1) (causal) / L*4*d*sum l^2 (non-causal)."""
+    lengths = [int(v) for v in lengths]
+    L, d, F_ = config.num_layers, config.d_model, config.ffn_dim
+    gemm = L * 2.0 * sum(lengths) * (4 * d * d + 2 * d * F_)
+    if config.causal:
+        attn = L * 2.0 * d * sum(v * (v + 1) for v in lengths)
+    else:
+        attn = L * 4.0 * d * sum(v * v for v in lengths)
+    return gemm, attn
