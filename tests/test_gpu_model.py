@@ -121,7 +121,7 @@ def test_c5_exact_route_full_length_sample():
         assert torch.isfinite(got).all()
         rows = got.reshape(-1, cfg.d_model)
         assert rows.mean(-1).abs().max().item() < 1e-3  # final LN with default gamma=1, beta=0
-        ref = linear_memory.linear_memory_forward(oracle, x[:1], mask[:1], q_chunk=4096)
+        ref = linear_memory.linear_memory_forward(oracle, x[:1], mask[:1], q_chunk=256)
         v = check_outputs(ref, got[:1])
         assert v.passed, f"{v.failed_elements} failed, max_abs={v.max_abs_error:.3g}"
 
@@ -132,6 +132,8 @@ def test_noncausal_and_general_mask():
     with torch.inference_mode():
         x, mask = generate_random_case(cfg, DEV, torch.float32, 7, 0.4)
         _assert_pass(oracle(x, mask), cand(x, mask), mask, cand)
+        # unpadded draw so every row the holey mask keeps carries N(0,1) input
+        x, _ = generate_random_case(cfg, DEV, torch.float32, 7, 0.0)
         g = torch.Generator(device=DEV).manual_seed(3)
         gmask = torch.rand(3, 320, generator=g, device=DEV) > 0.25
         gmask[:, 0] = True
