@@ -169,8 +169,9 @@ int launch_attn_hd(const void* q, const void* k, const void* v, const tj::AttnPa
     TJ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes));
     attr_set[dev] = true;
   }
-  dim3 grid((p.S + 127) / 128, B * p.H);
-  kern<<<grid, 192, Cfg::kSmemBytes, st>>>(tq, tk, tv, p);
+  const int q_tiles = (p.S + 127) / 128;
+  dim3 grid((q_tiles + 1) / 2, B * p.H);  // one CTA per pair of 128-query tiles
+  kern<<<grid, Cfg::kThreads, Cfg::kSmemBytes, st>>>(tq, tk, tv, p);
   TJ_CUDA(cudaGetLastError());
   return TJ_OK;
 }
