@@ -9,7 +9,7 @@
 #include <string>
 #include <vector>
 
-#include "../../include/tj.h"
+#include "tj.h"
 #include "tj_attention.cuh"
 #include "tj_common.cuh"
 #include "tj_gemm.cuh"

@@ -11,7 +11,9 @@
 //                  O_t += P_t V_j           (TS form: P_t read from TMEM)
 //   warps 0..3   softmax for query tile 0, warps 4..7 for tile 1: thread r
 //                owns row r; one pass over its S row (fp32, exp2 domain),
-//                writes P (fp16, packed 2 per column) over the S columns,
+//                writes P (fp16, packed 2 per column) to TMEM (own columns
+//                for head_dim <= 64, so S_t(j+1) overlaps this tile's
+//                exponentials; over S for head_dim 128),
 //                and rescales its O row in TMEM only when its running max
 //                grows by more than 2^8 (stale maxima keep p <= 256).
 //
@@ -48,7 +50,14 @@ struct AttnCfg {
   static constexpr int kTile = 128 * HD * 2;
   static constexpr int kStages = HD >= 128 ? 2 : (HD == 64 ? 4 : 6);
   static constexpr int kSmemBytes = 2 * kTile + kStages * 2 * kTile + 1024 + 256;
-  static constexpr int kTmemCols = 512;  // S0 | S1 | O0 | O1
+  static constexpr int kTmemCols = 512;
+  // TMEM columns.  HD <= 64: S0 S1 (fp32) | P0 P1 (fp16 pairs) | O0 O1, so the
+  // next S can be computed while P is still being consumed.  HD = 128: P
+  // overwrites the first half of S (S0 S1 | O0 O1 fills all 512 columns).
+  static constexpr bool kPSeparate = HD <= 64;
+  static constexpr int kColS = 0;
+  static constexpr int kColP = kPSeparate ? 256 : 0;
+  static constexpr int kColO = kPSeparate ? 384 : 256;
   static constexpr int kThreads = 320;
   static constexpr float kRescaleLog2 = 8.0f;
 };
@@ -87,7 +96,8 @@ __global__ void __launch_bounds__(320, 1)
   uint64_t* p_full = s_full + 2;     // [2]
   uint64_t* pv_done = p_full + 2;    // [2]
   uint64_t* o_final = pv_done + 2;   // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_final + 2);
+  uint64_t* s_free = o_final + 2;    // [2] softmax has read S_t into registers
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_free + 2);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -99,6 +109,7 @@ __global__ void __launch_bounds__(320, 1)
       mbar_init(p_full + i, 128);
       mbar_init(pv_done + i, 1);
       mbar_init(o_final + i, 1);
+      mbar_init(s_free + i, 128);
     }
     fence_mbar_init();
   }
@@ -144,46 +155,77 @@ __global__ void __launch_bounds__(320, 1)
       constexpr uint32_t idesc_pv = idesc_f16_f32(128, HD, false, true);
       const uint32_t q_addr = smem_u32(sQ);
       bool ok = mbar_wait(q_full, 0, p.err, kErrAttnMma);
-      for (int j = 0; j < n_kv && ok; ++j) {
-        const int st = j % ST;
-        if (!mbar_wait(kv_full + st, (j / ST) & 1, p.err, kErrAttnMma)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t k_addr = smem_u32(sKV + st * 2 * Cfg::kTile);
-        const uint32_t v_addr = k_addr + Cfg::kTile;
-        // S_t = Q_t K_j^T.  S_t's columns hold P_t(j-1), read by PV_t(j-1): wait for it.
-        for (int t = 0; t < 2; ++t) {
-          const int nkv_t = t == 0 ? nkv0 : nkv1;
-          if (j >= nkv_t) continue;
-          if (j > 0 && !mbar_wait(pv_done + t, (j - 1) & 1, p.err, kErrAttnMma)) { ok = false; break; }
-          tc_fence_after();
-          const uint32_t qa = q_addr + t * Cfg::kTile;
+      auto issue_s = [&](int t, int jj, uint32_t k_addr) {
+        const uint32_t qa = q_addr + t * Cfg::kTile;
 #pragma unroll
-          for (int ks = 0; ks < HD / 16; ++ks) {
-            const int atom = (ks * 16) / Cfg::kAtomCols;
-            const int within = ((ks * 16) % Cfg::kAtomCols) * 2;
-            const uint64_t ad = smem_desc(qa + atom * Cfg::kAtomBytes + within, 16, 8 * Cfg::kRowB, Cfg::kSw);
-            const uint64_t bd = smem_desc(k_addr + atom * Cfg::kAtomBytes + within, 16, 8 * Cfg::kRowB, Cfg::kSw);
-            umma_f16_ss(tmem + t * 128, ad, bd, idesc_qk, ks != 0);
-          }
-          umma_commit(s_full + t);
+        for (int ks = 0; ks < HD / 16; ++ks) {
+          const int atom = (ks * 16) / Cfg::kAtomCols;
+          const int within = ((ks * 16) % Cfg::kAtomCols) * 2;
+          const uint64_t ad = smem_desc(qa + atom * Cfg::kAtomBytes + within, 16, 8 * Cfg::kRowB, Cfg::kSw);
+          const uint64_t bd = smem_desc(k_addr + atom * Cfg::kAtomBytes + within, 16, 8 * Cfg::kRowB, Cfg::kSw);
+          umma_f16_ss(tmem + Cfg::kColS + t * 128, ad, bd, idesc_qk, ks != 0);
         }
-        if (!ok) break;
-        // O_t += P_t V_j, P_t from TMEM (fp16 pairs over S_t's first 64 columns)
-        for (int t = 0; t < 2; ++t) {
-          const int nkv_t = t == 0 ? nkv0 : nkv1;
-          if (j >= nkv_t) continue;
-          if (!mbar_wait(p_full + t, j & 1, p.err, kErrAttnMma)) { ok = false; break; }
-          tc_fence_after();
-          const uint32_t o_tmem = tmem + 256 + t * HD;
+        umma_commit(s_full + t);
+      };
+      auto issue_pv = [&](int t, int jj, uint32_t v_addr) {
+        const uint32_t o_tmem = tmem + Cfg::kColO + t * HD;
+        const uint32_t p_tmem = tmem + (Cfg::kPSeparate ? Cfg::kColP + t * 64 : Cfg::kColS + t * 128);
 #pragma unroll
-          for (int ks = 0; ks < 8; ++ks) {
-            const uint64_t bd = smem_desc(v_addr + ks * 16 * Cfg::kRowB, Cfg::kAtomBytes, 8 * Cfg::kRowB, Cfg::kSw);
-            umma_f16_ts(o_tmem, tmem + t * 128 + ks * 8, bd, idesc_pv, (j | ks) != 0);
-          }
-          umma_commit(pv_done + t);
-          if (j == nkv_t - 1) umma_commit(o_final + t);
+        for (int ks = 0; ks < 8; ++ks) {
+          const uint64_t bd = smem_desc(v_addr + ks * 16 * Cfg::kRowB, Cfg::kAtomBytes, 8 * Cfg::kRowB, Cfg::kSw);
+          umma_f16_ts(o_tmem, p_tmem + ks * 8, bd, idesc_pv, (jj | ks) != 0);
         }
-        umma_commit(kv_empty + st);
+        umma_commit(pv_done + t);
+        if (jj == (t == 0 ? nkv0 : nkv1) - 1) umma_commit(o_final + t);
+      };
+      auto kv_addr = [&](int jj) { return smem_u32(sKV + (jj % ST) * 2 * Cfg::kTile); };
+      if constexpr (Cfg::kPSeparate) {
+        // Lookahead order per step j: S_t(j+1) as soon as the softmax has read
+        // S_t(j), then PV_t(j) once P_t(j) is ready.
+        if (ok && (ok = mbar_wait(kv_full, 0, p.err, kErrAttnMma))) {
+          tc_fence_after();
+          for (int t = 0; t < 2; ++t)
+            if (0 < (t == 0 ? nkv0 : nkv1)) issue_s(t, 0, kv_addr(0));
+        }
+        for (int j = 0; j < n_kv && ok; ++j) {
+          if (j + 1 < n_kv) {
+            const int sn = (j + 1) % ST;
+            if (!mbar_wait(kv_full + sn, ((j + 1) / ST) & 1, p.err, kErrAttnMma)) { ok = false; break; }
+            for (int t = 0; t < 2 && ok; ++t) {
+              if (j + 1 >= (t == 0 ? nkv0 : nkv1)) continue;
+              if (!mbar_wait(s_free + t, j & 1, p.err, kErrAttnMma)) { ok = false; break; }
+              tc_fence_after();
+              issue_s(t, j + 1, kv_addr(j + 1));
+            }
+          }
+          for (int t = 0; t < 2 && ok; ++t) {
+            if (j >= (t == 0 ? nkv0 : nkv1)) continue;
+            if (!mbar_wait(p_full + t, j & 1, p.err, kErrAttnMma)) { ok = false; break; }
+            tc_fence_after();
+            issue_pv(t, j, kv_addr(j) + Cfg::kTile);
+          }
+          umma_commit(kv_empty + j % ST);
+        }
+      } else {
+        // P_t(j) lives in S_t's columns: S_t(j+1) must wait for PV_t(j).
+        for (int j = 0; j < n_kv && ok; ++j) {
+          const int st = j % ST;
+          if (!mbar_wait(kv_full + st, (j / ST) & 1, p.err, kErrAttnMma)) { ok = false; break; }
+          tc_fence_after();
+          for (int t = 0; t < 2 && ok; ++t) {
+            if (j >= (t == 0 ? nkv0 : nkv1)) continue;
+            if (j > 0 && !mbar_wait(pv_done + t, (j - 1) & 1, p.err, kErrAttnMma)) { ok = false; break; }
+            tc_fence_after();
+            issue_s(t, j, kv_addr(j));
+          }
+          for (int t = 0; t < 2 && ok; ++t) {
+            if (j >= (t == 0 ? nkv0 : nkv1)) continue;
+            if (!mbar_wait(p_full + t, j & 1, p.err, kErrAttnMma)) { ok = false; break; }
+            tc_fence_after();
+            issue_pv(t, j, kv_addr(j) + Cfg::kTile);
+          }
+          umma_commit(kv_empty + st);
+        }
       }
     }
   } else {
@@ -195,8 +237,9 @@ __global__ void __launch_bounds__(320, 1)
     const int qt = q0 + t;
     const int qrow = qt * 128 + r;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    const uint32_t s_col = tmem + lane_off + t * 128;
-    const uint32_t o_col = tmem + lane_off + 256 + t * HD;
+    const uint32_t s_col = tmem + lane_off + Cfg::kColS + t * 128;
+    const uint32_t p_col = tmem + lane_off + (Cfg::kPSeparate ? Cfg::kColP + t * 64 : Cfg::kColS + t * 128);
+    const uint32_t o_col = tmem + lane_off + Cfg::kColO + t * HD;
     const float sl2 = p.scale_log2;
     const uint8_t* kmask = general ? p.mask + (size_t)b * p.S : nullptr;
     float m_run = -INFINITY;  // running (possibly stale) max, log2 units
@@ -211,6 +254,10 @@ __global__ void __launch_bounds__(320, 1)
       tmem_ld32(s_col + 64, *reinterpret_cast<uint32_t(*)[32]>(s + 64));
       tmem_ld32(s_col + 96, *reinterpret_cast<uint32_t(*)[32]>(s + 96));
       tmem_ld_wait();
+      if constexpr (Cfg::kPSeparate) {
+        tc_fence_before();
+        mbar_arrive(s_free + t);  // S_t may now be overwritten by S_t(j+1)
+      }
       const int kbase = j * 128;
       const bool diag = p.causal && j == qt;
       const bool tail = kbase + 128 > len;
@@ -225,9 +272,14 @@ __global__ void __launch_bounds__(320, 1)
           if (dead) s[i] = __float_as_uint(-INFINITY);
         }
       }
-      float mx = -INFINITY;
+      // row max with 8 independent chains
+      float mx8[8];
 #pragma unroll
-      for (int i = 0; i < 128; ++i) mx = fmaxf(mx, __uint_as_float(s[i]));
+      for (int k = 0; k < 8; ++k) mx8[k] = __uint_as_float(s[k]);
+#pragma unroll
+      for (int i = 8; i < 128; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], __uint_as_float(s[i]));
+      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
       const float m_tile = mx * sl2;
       const bool grow = m_tile > m_run + Cfg::kRescaleLog2;
       float alpha = 1.0f;
@@ -235,7 +287,28 @@ __global__ void __launch_bounds__(320, 1)
         alpha = fast_exp2(m_run - m_tile);  // 0 when m_run = -inf
         m_run = m_tile;
       }
-      // rescale this row of O in TMEM (whole warp takes part if any lane needs it)
+      const float msub = m_run == -INFINITY ? 0.0f : m_run;
+      float sum8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      // P packs two fp16 per 32-bit column; the packed words overwrite s[]
+      // in place (word i only consumes s[2i], s[2i+1], both >= i).
+#pragma unroll
+      for (int i = 0; i < 64; ++i) {
+        const float p0 = fast_exp2(fmaf(__uint_as_float(s[2 * i]), sl2, -msub));
+        const float p1 = fast_exp2(fmaf(__uint_as_float(s[2 * i + 1]), sl2, -msub));
+        sum8[i & 7] += p0 + p1;
+        s[i] = pack_half2(p0, p1);
+      }
+      if constexpr (Cfg::kPSeparate) {
+        // P_t and O_t are free once PV_t(j-1) has retired
+        if (j > 0 && !mbar_wait(pv_done + t, (j - 1) & 1, p.err, kErrAttnSoftmax)) { ok = false; break; }
+        tc_fence_after();
+      }
+      tmem_st32(p_col, *reinterpret_cast<uint32_t(*)[32]>(s));
+      tmem_st32(p_col + 32, *reinterpret_cast<uint32_t(*)[32]>(s + 32));
+      const float rowsum = ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
+      l_run = l_run * alpha + rowsum;
+      // Rescale this row of O in TMEM (the whole warp takes part if any lane
+      // needs it).  PV_t(j-1) has retired, so O is stable.
       if (j > 0 && __any_sync(0xffffffffu, grow)) {
 #pragma unroll
         for (int c = 0; c < HD / 32; ++c) {
@@ -247,21 +320,6 @@ __global__ void __launch_bounds__(320, 1)
           tmem_st32(o_col + c * 32, o);
         }
       }
-      const float msub = m_run == -INFINITY ? 0.0f : m_run;
-      float rowsum = 0.0f;
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        uint32_t pk[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float p0 = fast_exp2(fmaf(__uint_as_float(s[64 * half + 2 * i]), sl2, -msub));
-          const float p1 = fast_exp2(fmaf(__uint_as_float(s[64 * half + 2 * i + 1]), sl2, -msub));
-          rowsum += p0 + p1;
-          pk[i] = pack_half2(p0, p1);
-        }
-        tmem_st32(s_col + 32 * half, pk);
-      }
-      l_run = l_run * alpha + rowsum;
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(p_full + t);
