@@ -116,6 +116,19 @@ TJ_API int tj_workspace_bytes(const TjModel* model, int batch, int seq_len, size
 TJ_API int tj_forward(TjModel* model, const float* x, const uint8_t* valid_mask, float* out, int batch, int seq_len,
                int route, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Allocation-free forward (no counterpart in the reference).  Same result as
+   tj_forward, but its scratch lives in a fixed device array inside this
+   library (TJ_NOALLOC_SCRATCH_BYTES per device, held until process exit)
+   instead of a caller workspace; for callers that cannot allocate device
+   memory on their call path.  Shapes whose scratch (tj_workspace_bytes)
+   exceeds the array are rejected with TJ_ERR_UNSUPPORTED.  The first call on
+   a device resolves the array's device address; make that first call before
+   any stream capture.  All calls share the one array: calls that overlap on
+   the GPU (different streams or threads) race. */
+#define TJ_NOALLOC_SCRATCH_BYTES (32u << 20)
+TJ_API int tj_forward_noalloc(TjModel* model, const float* x, const uint8_t* valid_mask, float* out, int batch,
+                              int seq_len, int route, void* stream);
+
 /* Reads (synchronously) and clears the model's device error word: 0 if no
    kernel's bounded wait expired since the last call. */
 TJ_API int tj_device_error(TjModel* model, int* code);

@@ -54,6 +54,7 @@ SIGNATURES = {
     "tj_workspace_bytes": (c_int, [c_void_p, c_int, c_int, POINTER(c_size_t)]),
     "tj_forward": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_size_t,
                            c_void_p]),
+    "tj_forward_noalloc": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]),
     "tj_device_error": (c_int, [c_void_p, POINTER(c_int)]),
     "tj_profile_begin": (c_int, [c_void_p, c_int]),
     "tj_profile_end": (c_int, [c_void_p, POINTER(ctypes.c_double), POINTER(ctypes.c_longlong)]),

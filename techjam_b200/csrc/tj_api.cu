@@ -523,6 +523,58 @@ int tj_forward(TjModel* m, const float* x, const uint8_t* mask, float* out, int 
   return TJ_OK;
 }
 
+// ------------------------------------------------------------------ allocation-free forward
+// Some callers cannot call cudaMalloc on their call path: a host application
+// or serving runtime that owns a fixed device-memory budget and forbids
+// allocation after start-up, or a latency-critical path where cudaMalloc's
+// implicit device synchronisation is not acceptable.  tj_forward_noalloc
+// gives them the same forward with its scratch in this fixed array, so the
+// call itself allocates nothing.  Every device that loads this library holds
+// the array (TJ_NOALLOC_SCRATCH_BYTES) until the process exits.
+static __device__ __align__(256) uint8_t g_noalloc_scratch[TJ_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[64] = {};  // device address of g_noalloc_scratch, per device
+
+// Host code cannot use g_noalloc_scratch's name as a device pointer (it is a
+// host-side stand-in); resolve the real address once per device, with that
+// device current.
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  TJ_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fail(TJ_ERR_NO_DEVICE, "device index %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_addr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr)
+      return fail(TJ_ERR_CUDA, "cudaGetSymbolAddress(noalloc scratch): %s", cudaGetErrorString(e));
+    g_noalloc_addr[dev] = p;
+  }
+  *out = g_noalloc_addr[dev];
+  return TJ_OK;
+}
+}  // namespace
+
+int tj_forward_noalloc(TjModel* m, const float* x, const uint8_t* mask, float* out, int B, int S, int route,
+                       void* stream) {
+  if (!m) return fail(TJ_ERR_INVALID, "null model");
+  if (B <= 0 || S <= 0) return fail(TJ_ERR_INVALID, "batch and seq_len must be positive");
+  const size_t need = carve(m->cfg, B, S, nullptr, nullptr);
+  if (need > (size_t)TJ_NOALLOC_SCRATCH_BYTES)
+    return fail(TJ_ERR_UNSUPPORTED,
+                "batch=%d seq_len=%d needs %zu bytes of scratch; tj_forward_noalloc has %u (use tj_forward "
+                "with a caller workspace)",
+                B, S, need, (unsigned)TJ_NOALLOC_SCRATCH_BYTES);
+  void* scratch = nullptr;
+  TJ_CHECK(noalloc_scratch(&scratch));
+  // The array keeps the previous call's contents (possibly for another shape,
+  // carved differently); tj_forward expects zero-filled scratch.
+  TJ_CUDA(cudaMemsetAsync(scratch, 0, need, static_cast<cudaStream_t>(stream)));
+  return tj_forward(m, x, mask, out, B, S, route, scratch, need, stream);
+}
+
 int tj_profile_begin(TjModel* m, int max_launches) {
   if (!m || max_launches <= 0) return fail(TJ_ERR_INVALID, "bad profile arguments");
   if ((int)m->prof_cls.size() < max_launches) {
