@@ -4,10 +4,13 @@
 //
 // One CTA per SM.  Warp 0 issues TMA loads into a STAGES-deep shared-memory
 // ring, warp 1 (one thread) issues tcgen05.mma into one of two TMEM
-// accumulators, warps 2..5 drain the other accumulator through the epilogue
-// (tcgen05.ld -> bias / GELU / residual / head scatter -> global).  M tiles
-// that hold no valid token (right padding) are dropped up front: the kernel
-// walks a compact device-side list of live 128-row tiles.
+// accumulators, warps 2..9 drain the other accumulator through the epilogue
+// (tcgen05.ld -> bias / GELU / residual / head scatter -> global).  Two
+// epilogue warps share each TMEM lane quarter, one per half of the tile's
+// columns, and each prefetches the next 32-column chunk's residual while the
+// current chunk is computed.  M tiles that hold no valid token (right
+// padding) are dropped up front: the kernel walks a compact device-side list
+// of live 128-row tiles.
 #pragma once
 #include "tj_common.cuh"
 
@@ -47,7 +50,8 @@ struct GemmCfg {
   static constexpr int kStages = (200 * 1024) / kStageBytes;
   static constexpr int kTmemCols = 2 * BN;  // double-buffered accumulator
   static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
-  static constexpr int kThreads = 192;
+  static constexpr int kThreads = 320;  // TMA warp, MMA warp, 8 epilogue warps
+  static constexpr int kEpiThreads = 256;
 };
 
 TJ_DEV bool row_is_valid(const GemmParams& p, int row) {
@@ -60,17 +64,35 @@ TJ_DEV bool row_is_valid(const GemmParams& p, int row) {
 
 TJ_DEV float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752440f)); }
 
+// DRAM operand of an epilogue chunk (one row x 32 columns): the residual.
+// (The bias row is shared by every row of the tile and stays L1-resident.)
+struct ChunkOperands {
+  float4 resid[8];
+};
+
 template <int EPI>
-TJ_DEV void epilogue_chunk(const GemmParams& p, int row, bool valid, int col0, const uint32_t (&acc)[32]) {
+TJ_DEV void load_chunk_operands(const GemmParams& p, int row, bool valid, int col0, ChunkOperands& o) {
+  if constexpr (EPI == kEpiResid) {
+    if (valid) {
+      const float4* src = reinterpret_cast<const float4*>(p.resid + (size_t)row * p.N + col0);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o.resid[j] = src[j];
+    }
+  }
+}
+
+template <int EPI>
+TJ_DEV void epilogue_chunk(const GemmParams& p, int row, bool valid, int col0, const uint32_t (&acc)[32],
+                           const ChunkOperands& o) {
   float v[32];
   if (valid) {
 #pragma unroll
-    for (int j = 0; j < 32; j += 4) {
-      const float4 bb = __ldg(reinterpret_cast<const float4*>(p.bias + col0 + j));
-      v[j] = __uint_as_float(acc[j]) + bb.x;
-      v[j + 1] = __uint_as_float(acc[j + 1]) + bb.y;
-      v[j + 2] = __uint_as_float(acc[j + 2]) + bb.z;
-      v[j + 3] = __uint_as_float(acc[j + 3]) + bb.w;
+    for (int j = 0; j < 8; ++j) {
+      const float4 bb = __ldg(reinterpret_cast<const float4*>(p.bias + col0) + j);
+      v[4 * j] = __uint_as_float(acc[4 * j]) + bb.x;
+      v[4 * j + 1] = __uint_as_float(acc[4 * j + 1]) + bb.y;
+      v[4 * j + 2] = __uint_as_float(acc[4 * j + 2]) + bb.z;
+      v[4 * j + 3] = __uint_as_float(acc[4 * j + 3]) + bb.w;
     }
   } else {
 #pragma unroll
@@ -79,11 +101,10 @@ TJ_DEV void epilogue_chunk(const GemmParams& p, int row, bool valid, int col0, c
   if constexpr (EPI == kEpiResid) {
     float* dst = p.out32 + (size_t)row * p.N + col0;
     if (valid) {
-      const float* src = p.resid + (size_t)row * p.N + col0;
 #pragma unroll
-      for (int j = 0; j < 32; j += 4) {
-        const float4 r = *reinterpret_cast<const float4*>(src + j);
-        v[j] += r.x; v[j + 1] += r.y; v[j + 2] += r.z; v[j + 3] += r.w;
+      for (int j = 0; j < 8; ++j) {
+        v[4 * j] += o.resid[j].x; v[4 * j + 1] += o.resid[j].y;
+        v[4 * j + 2] += o.resid[j].z; v[4 * j + 3] += o.resid[j].w;
       }
     }
 #pragma unroll
@@ -122,7 +143,7 @@ TJ_DEV void epilogue_chunk(const GemmParams& p, int row, bool valid, int col0, c
 }
 
 template <int BN, int EPI>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(320, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
                    const GemmParams p) {
   using Cfg = GemmCfg<BN>;
@@ -141,7 +162,7 @@ __global__ void __launch_bounds__(192, 1)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) { mbar_init(full + i, 1); mbar_init(empty + i, 1); }
-    for (int i = 0; i < 2; ++i) { mbar_init(acc_full + i, 1); mbar_init(acc_empty + i, 128); }
+    for (int i = 0; i < 2; ++i) { mbar_init(acc_full + i, 1); mbar_init(acc_empty + i, Cfg::kEpiThreads); }
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -209,26 +230,34 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else if (warp >= 2) {
     // ------------------------------------------------------------ epilogue
-    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    const int quarter = warp & 3;         // TMEM lane quarter this warp may access
+    const int half = (warp - 2) >> 2;     // which half of the tile's columns
+    constexpr int kChunks = BN / 64;      // 32-column chunks per half
     const int row_in_tile = quarter * 32 + lane;
     int abuf = 0;
     uint32_t aphase = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
       const int mt = __ldg(p.tile_list + t / n_tiles);
       const int nt = t % n_tiles;
-      if (!mbar_wait(acc_full + abuf, aphase, p.err, kErrGemmEpilogue)) break;
-      tc_fence_after();
       const int row = mt * kGemmBM + row_in_tile;
       const bool in_range = row < p.M;
       const bool valid = row_is_valid(p, row);
-      const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + abuf * BN;
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
+      const int colh = nt * BN + half * (BN / 2);
+      // operands of the first chunk are fetched while the MMAs still run
+      ChunkOperands ops[2];
+      if (in_range && colh < p.N) load_chunk_operands<EPI>(p, row, valid, colh, ops[0]);
+      if (!mbar_wait(acc_full + abuf, aphase, p.err, kErrGemmEpilogue)) break;
+      tc_fence_after();
+      const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + abuf * BN + half * (BN / 2);
+#pragma unroll
+      for (int c = 0; c < kChunks; ++c) {
+        const int col0 = colh + c * 32;
+        if (c + 1 < kChunks && in_range && col0 + 32 < p.N)
+          load_chunk_operands<EPI>(p, row, valid, col0 + 32, ops[(c + 1) & 1]);
         uint32_t acc[32];
         tmem_ld32(taddr + c * 32, acc);
         tmem_ld_wait();
-        const int col0 = nt * BN + c * 32;
-        if (in_range && col0 < p.N) epilogue_chunk<EPI>(p, row, valid, col0, acc);
+        if (in_range && col0 < p.N) epilogue_chunk<EPI>(p, row, valid, col0, acc, ops[c & 1]);
       }
       tc_fence_before();
       mbar_arrive(acc_empty + abuf);
