@@ -104,10 +104,13 @@ TJ_API int tj_model_destroy(TjModel* model);
 TJ_API int tj_model_load_layer(TjModel* model, int layer, const TjLayerParams* params, void* stream);
 TJ_API int tj_model_load_final_norm(TjModel* model, const float* weight, const float* bias, void* stream);
 
-/* Bytes of scratch tj_forward needs for [batch, seq_len] inputs.  The
-   workspace must be zero-filled before its first use (afterwards tj_forward
-   only ever writes finite values into it). */
-TJ_API int tj_workspace_bytes(const TjModel* model, int batch, int seq_len, size_t* bytes);
+/* Bytes of scratch tj_forward needs for [batch, seq_len] inputs and the given
+   TjAttentionRoute (the polynomial route adds its per-chunk state snapshots
+   when the shape can take it: causal, head_dim 64, seq_len a multiple of 512
+   above the 4096-token exact prefix; TJ_ROUTE_AUTO only from 16384 tokens).
+   The workspace must be zero-filled before its first use (afterwards
+   tj_forward only ever writes finite values into it). */
+TJ_API int tj_workspace_bytes(const TjModel* model, int batch, int seq_len, int route, size_t* bytes);
 
 /* out[B,S,d] = encoder(x[B,S,d]) with the reference's padding semantics:
    valid_mask[B,S] (1 byte per token, nullable = all valid); padded output rows
@@ -191,6 +194,25 @@ TJ_API int tj_gemm_f16(const void* a, const void* w, const float* bias, int batc
 TJ_API int tj_attention_f16(const void* q, const void* k, const void* v, void* ctx, int batch, int heads, int seq_len,
                      int head_dim, int causal, const int* lengths, const uint8_t* mask, const uint8_t* general,
                      int* err, void* stream);
+
+/* Guarded polynomial causal attention over Q,K,V fp16 [B,H,S,64] with no
+   padding (lengths[b] == S), replacing PolyOrFlashSelfAttention.forward +
+   poly_attention_forward (src/implementations/extreme.py:276-319,
+   poly_attention.py:21-83; algorithm poly_reference.py:61-265; guard
+   poly_guard.py:65-102): a device-side score-range check admits the route
+   (sigma <= 0.40, max |s| <= 10, unpadded); queries < exact_prefix, or all of
+   them when not admitted, take the exact flash kernel.  The workspace starts
+   with a TjPolyStatus describing the last call. */
+typedef struct TjPolyStatus {
+  int admit;             /* 1 = polynomial route ran, 0 = exact fallback */
+  float c0, c1, c2;      /* Hermite coefficients used */
+  float sigma;           /* std of the sampled scaled scores */
+  float max_abs;         /* max |scaled score| in the sample */
+} TjPolyStatus;
+TJ_API int tj_poly_workspace_bytes(int batch, int heads, int seq_len, int exact_prefix, size_t* bytes);
+TJ_API int tj_poly_attention_f16(const void* q, const void* k, const void* v, void* ctx, const int* lengths,
+                                 int batch, int heads, int seq_len, int exact_prefix, void* workspace,
+                                 size_t workspace_bytes, int* err, void* stream);
 
 #ifdef __cplusplus
 }

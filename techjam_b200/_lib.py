@@ -51,7 +51,7 @@ SIGNATURES = {
     "tj_model_destroy": (c_int, [c_void_p]),
     "tj_model_load_layer": (c_int, [c_void_p, c_int, POINTER(TjLayerParams), c_void_p]),
     "tj_model_load_final_norm": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p]),
-    "tj_workspace_bytes": (c_int, [c_void_p, c_int, c_int, POINTER(c_size_t)]),
+    "tj_workspace_bytes": (c_int, [c_void_p, c_int, c_int, c_int, POINTER(c_size_t)]),
     "tj_forward": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_size_t,
                            c_void_p]),
     "tj_forward_noalloc": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]),
@@ -66,6 +66,9 @@ SIGNATURES = {
     "tj_gemm_f16": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p,
                             c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                             c_void_p]),
+    "tj_poly_workspace_bytes": (c_int, [c_int, c_int, c_int, c_int, POINTER(c_size_t)]),
+    "tj_poly_attention_f16": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int,
+                                      c_void_p, c_size_t, c_void_p, c_void_p]),
     "tj_attention_f16": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int,
                                  c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
 }

@@ -14,6 +14,7 @@
 #include "tj_common.cuh"
 #include "tj_gemm.cuh"
 #include "tj_misc.cuh"
+#include "tj_poly.cuh"
 
 namespace {
 
@@ -235,9 +236,28 @@ struct Workspace {
   __half* k;
   __half* v;    // [B, H, S, hd] each
   __half* ff;   // [M, F]
+  tj::PolyCtl* poly_ctl;  // polynomial route (null when the route cannot run)
+  __half* poly_snap;
 };
 
-size_t carve(const TjConfig& c, int B, int S, uint8_t* base, Workspace* w) {
+// Exact prefix of the polynomial route (the reference's EXACT_PREFIX) and the
+// shortest sequence TJ_ROUTE_AUTO sends down that route.
+constexpr int kPolyExactPrefix = 4096;
+constexpr int kPolyAutoMinSeq = 16384;
+
+// Can the polynomial route run for this shape under this route request?
+bool poly_eligible(const TjConfig& c, int S, int route) {
+  if (route == TJ_ROUTE_EXACT || !c.causal || c.d_model / c.num_heads != 64) return false;
+  if (S % tj::kPolyChunk != 0 || S <= kPolyExactPrefix) return false;
+  return route == TJ_ROUTE_POLY || S >= kPolyAutoMinSeq;
+}
+
+size_t poly_snap_elems(int BH, int S) {
+  const size_t n_snap = (size_t)(S / tj::kPolyChunk - kPolyExactPrefix / tj::kPolyChunk);
+  return (size_t)BH * n_snap * tj::kPolyN * tj::kPolyFeat;
+}
+
+size_t carve(const TjConfig& c, int B, int S, int route, uint8_t* base, Workspace* w) {
   const size_t M = (size_t)B * S;
   const size_t tiles = (M + 127) / 128;
   size_t off = 0;
@@ -257,6 +277,12 @@ size_t carve(const TjConfig& c, int B, int S, uint8_t* base, Workspace* w) {
   t.k = reinterpret_cast<__half*>(take(2 * M * c.d_model));
   t.v = reinterpret_cast<__half*>(take(2 * M * c.d_model));
   t.ff = reinterpret_cast<__half*>(take(2 * M * c.ffn_dim));
+  t.poly_ctl = nullptr;
+  t.poly_snap = nullptr;
+  if (poly_eligible(c, S, route)) {
+    t.poly_ctl = reinterpret_cast<tj::PolyCtl*>(take(sizeof(tj::PolyCtl)));
+    t.poly_snap = reinterpret_cast<__half*>(take(2 * poly_snap_elems(B * c.num_heads, S)));
+  }
   if (w) *w = t;
   return off;
 }
@@ -301,6 +327,7 @@ namespace {
 // when profiling is active.
 template <class F>
 int timed_launch(TjModel* m, int cls, int kernels, cudaStream_t st, F&& launch) {
+  if (m == nullptr) return launch();  // building-block call: no model to count or profile
   const bool rec = m->prof_on && m->prof_n < m->prof_max;
   if (rec) TJ_CUDA(cudaEventRecord(m->prof_ev[2 * m->prof_n], st));
   const int s = launch();
@@ -313,6 +340,62 @@ int timed_launch(TjModel* m, int cls, int kernels, cudaStream_t st, F&& launch) 
   }
   return TJ_OK;
 }
+// Polynomial route for one layer: guard -> (exact prefix | whole sequence if
+// not admitted) on the flash kernel -> state update -> apply.  All admission
+// decisions stay on the device.
+int launch_poly_route(const __half* q, const __half* k, const __half* v, __half* ctx, const int* lengths, int B,
+                      int H, int S, int d_model, int exact_prefix, tj::PolyCtl* ctl, __half* snap, TjModel* m,
+                      const tj::AttnParams& ap_in, cudaStream_t st) {
+  tj::PolyParams pp{};
+  pp.q = q; pp.k = k; pp.v = v; pp.ctx = ctx; pp.snap = snap; pp.ctl = ctl; pp.lengths = lengths;
+  pp.B = B; pp.H = H; pp.S = S; pp.d_model = d_model;
+  pp.prefix_chunks = exact_prefix / tj::kPolyChunk;
+  pp.scale = 0.125f;  // 64^-0.5
+  pp.err = ap_in.err;
+  const int n_chunks = S / tj::kPolyChunk;
+  if (pp.prefix_chunks < 1 || pp.prefix_chunks >= n_chunks || exact_prefix % tj::kPolyChunk)
+    return fail(TJ_ERR_UNSUPPORTED, "polynomial route needs 512 <= exact prefix < seq_len, multiple of 512");
+  TJ_CHECK(timed_launch(m, TJ_K_POLY, 2, st, [&]() -> int {
+    TJ_CUDA(cudaMemsetAsync(ctl, 0, sizeof(tj::PolyCtl), st));
+    tj::poly_guard_kernel<<<dim3(tj::kPolySample / 64, B * H), 256, 0, st>>>(pp);
+    TJ_CUDA(cudaGetLastError());
+    tj::poly_guard_finalize<<<1, 1, 0, st>>>(pp);
+    TJ_CUDA(cudaGetLastError());
+    return TJ_OK;
+  }));
+  tj::AttnParams ap = ap_in;
+  ap.poly_admit = &ctl->admit;
+  ap.exact_pairs = exact_prefix / 256;
+  TJ_CHECK(timed_launch(m, TJ_K_ATTN, 1, st, [&] { return launch_attention(q, k, v, 64, ap, B, st); }));
+  const uint64_t rows = (uint64_t)B * H * S;
+  CUtensorMap tq, tk, tv, tsn;
+  TJ_CHECK(make_map_f16(&tq, q, rows, 64, 128, 64, 128));
+  TJ_CHECK(make_map_f16(&tk, k, rows, 64, 128, 64, 128));
+  TJ_CHECK(make_map_f16(&tv, v, rows, 64, 128, 64, 128));
+  const uint64_t snap_rows = (uint64_t)B * H * (n_chunks - pp.prefix_chunks) * tj::kPolyN;
+  TJ_CHECK(make_map_f16(&tsn, snap, snap_rows, tj::kPolyFeat, tj::kPolyN, 64, 128));
+  static bool attr_set[64] = {};
+  int dev = 0;
+  TJ_CUDA(cudaGetDevice(&dev));
+  if (!attr_set[dev]) {
+    TJ_CUDA(cudaFuncSetAttribute(tj::poly_update_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, tj::kUpdSmem));
+    TJ_CUDA(cudaFuncSetAttribute(tj::poly_apply_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, tj::kAppSmem));
+    attr_set[dev] = true;
+  }
+  TJ_CHECK(timed_launch(m, TJ_K_POLY, 1, st, [&]() -> int {
+    tj::poly_update_kernel<<<dim3(tj::kPolyFeatBlocks, B * H), 192, tj::kUpdSmem, st>>>(tk, tv, pp);
+    TJ_CUDA(cudaGetLastError());
+    return TJ_OK;
+  }));
+  TJ_CHECK(timed_launch(m, TJ_K_POLY, 1, st, [&]() -> int {
+    tj::poly_apply_kernel<<<dim3((n_chunks - pp.prefix_chunks) * 4, B * H), 192, tj::kAppSmem, st>>>(tq, tk, tv, tsn,
+                                                                                                   pp);
+    TJ_CUDA(cudaGetLastError());
+    return TJ_OK;
+  }));
+  return TJ_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -425,10 +508,10 @@ int tj_model_load_final_norm(TjModel* m, const float* w, const float* b, void* s
   return TJ_OK;
 }
 
-int tj_workspace_bytes(const TjModel* m, int B, int S, size_t* bytes) {
+int tj_workspace_bytes(const TjModel* m, int B, int S, int route, size_t* bytes) {
   if (!m || !bytes) return fail(TJ_ERR_INVALID, "null argument");
   if (B < 0 || S < 0) return fail(TJ_ERR_INVALID, "negative shape");
-  *bytes = carve(m->cfg, B, S, nullptr, nullptr);
+  *bytes = carve(m->cfg, B, S, route, nullptr, nullptr);
   return TJ_OK;
 }
 
@@ -444,10 +527,10 @@ int tj_forward(TjModel* m, const float* x, const uint8_t* mask, float* out, int 
   if (!m || !x || !out || !ws) return fail(TJ_ERR_INVALID, "null argument");
   if (B <= 0 || S <= 0) return fail(TJ_ERR_INVALID, "batch and seq_len must be positive");
   if (x == out) return fail(TJ_ERR_INVALID, "x and out must not alias");
-  if (route != TJ_ROUTE_EXACT && route != TJ_ROUTE_AUTO)
-    return fail(TJ_ERR_UNSUPPORTED, "attention route %d not available in this build", route);
+  if (route != TJ_ROUTE_EXACT && route != TJ_ROUTE_AUTO && route != TJ_ROUTE_POLY)
+    return fail(TJ_ERR_INVALID, "unknown attention route %d", route);
   const TjConfig& c = m->cfg;
-  const size_t need = carve(c, B, S, nullptr, nullptr);
+  const size_t need = carve(c, B, S, route, nullptr, nullptr);
   if (ws_bytes < need) return fail(TJ_ERR_INVALID, "workspace %zu bytes < required %zu", ws_bytes, need);
   if ((reinterpret_cast<uintptr_t>(ws) & 255) != 0) return fail(TJ_ERR_INVALID, "workspace not 256-byte aligned");
   if ((long long)B * S > (1LL << 31) / 128) return fail(TJ_ERR_UNSUPPORTED, "batch*seq_len too large");
@@ -458,7 +541,7 @@ int tj_forward(TjModel* m, const float* x, const uint8_t* mask, float* out, int 
   if (dev != m->device) return fail(TJ_ERR_INVALID, "model lives on device %d, current device is %d", m->device, dev);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   Workspace w;
-  carve(c, B, S, static_cast<uint8_t*>(ws), &w);
+  carve(c, B, S, route, static_cast<uint8_t*>(ws), &w);
   const int d = c.d_model, H = c.num_heads, hd = d / H, F = c.ffn_dim;
   const int M = B * S;
 
@@ -499,8 +582,14 @@ int tj_forward(TjModel* m, const float* x, const uint8_t* mask, float* out, int 
     // packed QKV projection -> Q, K, V [B, H, S, hd]
     gp.N = 3 * d; gp.K = d; gp.bias = L.bqkv;
     TJ_CHECK(timed_launch(m, TJ_K_QKV, 1, st, [&] { return launch_gemm_epi(tj::kEpiQKV, w.act, L.wqkv, gp, di.sms, st); }));
-    // attention -> ctx (reuses act)
-    TJ_CHECK(timed_launch(m, TJ_K_ATTN, 1, st, [&] { return launch_attention(w.q, w.k, w.v, hd, ap, B, st); }));
+    // attention -> ctx (reuses act): exact flash, or the guarded polynomial
+    // route (device-side guard; the flash kernel then covers the exact prefix)
+    if (w.poly_ctl != nullptr) {
+      TJ_CHECK(launch_poly_route(w.q, w.k, w.v, w.act, w.lengths, B, H, S, d, kPolyExactPrefix, w.poly_ctl,
+                                 w.poly_snap, m, ap, st));
+    } else {
+      TJ_CHECK(timed_launch(m, TJ_K_ATTN, 1, st, [&] { return launch_attention(w.q, w.k, w.v, hd, ap, B, st); }));
+    }
     // out projection + residual -> out (fp32 residual stream)
     gp.N = d; gp.K = d; gp.bias = L.bo; gp.out32 = out; gp.resid = resid_in;
     TJ_CHECK(timed_launch(m, TJ_K_OUT, 1, st, [&] { return launch_gemm_epi(tj::kEpiResid, w.act, L.wo, gp, di.sms, st); }));
@@ -561,7 +650,7 @@ int tj_forward_noalloc(TjModel* m, const float* x, const uint8_t* mask, float* o
                        void* stream) {
   if (!m) return fail(TJ_ERR_INVALID, "null model");
   if (B <= 0 || S <= 0) return fail(TJ_ERR_INVALID, "batch and seq_len must be positive");
-  const size_t need = carve(m->cfg, B, S, nullptr, nullptr);
+  const size_t need = carve(m->cfg, B, S, route, nullptr, nullptr);
   if (need > (size_t)TJ_NOALLOC_SCRATCH_BYTES)
     return fail(TJ_ERR_UNSUPPORTED,
                 "batch=%d seq_len=%d needs %zu bytes of scratch; tj_forward_noalloc has %u (use tj_forward "
@@ -573,6 +662,36 @@ int tj_forward_noalloc(TjModel* m, const float* x, const uint8_t* mask, float* o
   // carved differently); tj_forward expects zero-filled scratch.
   TJ_CUDA(cudaMemsetAsync(scratch, 0, need, static_cast<cudaStream_t>(stream)));
   return tj_forward(m, x, mask, out, B, S, route, scratch, need, stream);
+}
+
+int tj_poly_workspace_bytes(int B, int H, int S, int exact_prefix, size_t* bytes) {
+  if (!bytes || B <= 0 || H <= 0 || S <= 0) return fail(TJ_ERR_INVALID, "bad arguments");
+  if (S % tj::kPolyChunk || exact_prefix % tj::kPolyChunk || exact_prefix < tj::kPolyChunk || exact_prefix >= S)
+    return fail(TJ_ERR_UNSUPPORTED, "polynomial route needs seq_len and exact_prefix multiples of 512, 512 <= prefix < seq_len");
+  const size_t n_snap = (size_t)(S - exact_prefix) / tj::kPolyChunk;
+  *bytes = align_up(sizeof(tj::PolyCtl), 256) + 2 * (size_t)B * H * n_snap * tj::kPolyN * tj::kPolyFeat;
+  return TJ_OK;
+}
+
+int tj_poly_attention_f16(const void* q, const void* k, const void* v, void* ctx, const int* lengths, int B, int H,
+                          int S, int exact_prefix, void* ws, size_t ws_bytes, int* err, void* stream) {
+  if (!q || !k || !v || !ctx || !lengths || !ws || !err) return fail(TJ_ERR_INVALID, "null argument");
+  size_t need = 0;
+  TJ_CHECK(tj_poly_workspace_bytes(B, H, S, exact_prefix, &need));
+  if (ws_bytes < need) return fail(TJ_ERR_INVALID, "workspace %zu bytes < required %zu", ws_bytes, need);
+  if ((reinterpret_cast<uintptr_t>(ws) & 255) != 0) return fail(TJ_ERR_INVALID, "workspace not 256-byte aligned");
+  DeviceInfo di;
+  TJ_CHECK(device_info(&di));
+  auto* ctl = static_cast<tj::PolyCtl*>(ws);
+  auto* snap = reinterpret_cast<__half*>(static_cast<uint8_t*>(ws) + align_up(sizeof(tj::PolyCtl), 256));
+  tj::AttnParams ap{};
+  ap.lengths = lengths; ap.mask = nullptr; ap.general = nullptr; ap.ctx = static_cast<__half*>(ctx);
+  ap.S = S; ap.H = H; ap.d_model = H * 64; ap.causal = 1;
+  ap.scale_log2 = (float)(0.125 * 1.4426950408889634);
+  ap.err = err;
+  return launch_poly_route(static_cast<const __half*>(q), static_cast<const __half*>(k),
+                           static_cast<const __half*>(v), static_cast<__half*>(ctx), lengths, B, H, S, H * 64,
+                           exact_prefix, ctl, snap, nullptr, ap, static_cast<cudaStream_t>(stream));
 }
 
 int tj_profile_begin(TjModel* m, int max_launches) {

@@ -37,6 +37,10 @@ struct AttnParams {
   int causal;
   float scale_log2;        // head_dim^-0.5 * log2(e)
   int* err;
+  // Polynomial route: when *poly_admit != 0 only query pairs < exact_pairs
+  // (the exact prefix) are computed here; null = every query.
+  const int* poly_admit;
+  int exact_pairs;
 };
 
 template <int HD>
@@ -77,6 +81,8 @@ __global__ void __launch_bounds__(320, 1)
   const int q0 = 2 * pair;
   if (q0 * 128 >= len) return;
   if (error_raised(p.err)) return;
+  if (p.poly_admit != nullptr && pair >= p.exact_pairs && *reinterpret_cast<const volatile int*>(p.poly_admit) != 0)
+    return;
   const bool has1 = (q0 + 1) * 128 < len;
   const int kv_all = (len + 127) / 128;
   const int nkv0 = p.causal ? q0 + 1 : kv_all;

@@ -1,0 +1,613 @@
+// Guarded degree-2 polynomial (Hermite/Taylor-exp) causal linear attention
+// for long unpadded sequences, head_dim 64.
+//
+// Algorithm (the reference's poly_linear_attention): keys in EARLIER 512-token
+// chunks are weighted by w(s) = c0 + c1 s + c2 s^2 (s = q.k * scale), keys in
+// the SAME chunk by the exact exp(s) with the causal triangle, queries in the
+// first `exact_prefix` tokens by exact softmax (the flash kernel).
+//
+// B200 formulation.  With the 4224-wide feature maps
+//     phi_k(k) = [ scale k_i k_j (4096) | sqrt(scale) k_i (64) | 1 | 0 x 63 ]
+//     phi_q(q) = [ c2 scale q_i q_j     | c1 sqrt(scale) q_i   | c0 | 0 ... ]
+// phi_q(q) . phi_k(k) = w(q.k * scale), so for every query of chunk c
+//     [num | den] = phi_q(q) @ S_c + sum_{j in chunk, j <= i} exp(s_ij) [v_j | 1]
+// where S_c = sum over keys before chunk c of phi_k(k)^T [v | 1]  (4224 x 65).
+// A constant "ones" B tile makes the denominator column 64 of the same
+// accumulator, so numerator and denominator of all three polynomial orders
+// come out of one N=80 tensor-core accumulation.
+//
+//   poly_guard_kernel/poly_guard_finalize  score std (sigma) and max |s| over a
+//       fixed strided sample of 512 rows per head -> PolyCtl (admit flag and
+//       Hermite coefficients), on the device: no host synchronisation.  Every
+//       poly kernel exits at once unless admitted; the flash kernel then covers
+//       the whole sequence instead of only the exact prefix.
+//   poly_update_kernel  one CTA per (128-feature block, head): per 128-token
+//       sub-chunk it builds phi_k on the CUDA cores into shared memory and
+//       accumulates phi_k^T [v | 1] in TMEM (double-buffered per chunk); the
+//       running state stays in registers (fp32) and after every chunk the
+//       MEAN state S_c / (512 c) is stored as fp16 (keeps the fp16 snapshot in
+//       range however long the sequence).
+//   poly_apply_kernel   one CTA per (128-query block, head): phi_q(q) @ S_c
+//       over 33 feature blocks (K = 4224) plus the exact-exp diagonal block,
+//       then out = (512c * inter + diag)[:64] / (512c * inter + diag)[64].
+#pragma once
+#include "tj_common.cuh"
+
+namespace tj {
+
+constexpr int kPolyChunk = 512;
+constexpr int kPolyFeat = 4224;       // 4096 + 64 + 1, padded to 33 blocks of 128
+constexpr int kPolyFeatBlocks = 33;
+constexpr int kPolyN = 80;            // 64 numerator + 1 denominator, padded to N % 16 == 0
+constexpr int kPolySample = 512;      // rows per head in the guard's sample
+constexpr float kPolySigmaCeiling = 0.40f;
+constexpr float kPolyMaxScore = 10.0f;  // exp(s) of the diagonal block stays < fp16 max
+
+struct PolyCtl {
+  int admit;  // 1: polynomial route, 0: exact route
+  float c0, c1, c2;
+  float sigma;
+  float max_abs;
+  double sum, sumsq, maxv;  // guard accumulators
+};
+
+struct PolyParams {
+  const __half* q;  // [B, H, S, 64]
+  const __half* k;
+  const __half* v;
+  __half* ctx;      // [B*S, d_model]
+  __half* snap;     // [B*H][n_snap][80][4224] fp16 mean states
+  PolyCtl* ctl;
+  const int* lengths;
+  int B, H, S, d_model;
+  int prefix_chunks;  // exact prefix / 512
+  float scale;        // head_dim^-0.5
+  int* err;
+};
+
+// ------------------------------------------------------------------ guard
+// blockIdx.y = b*H + h; blockIdx.x = block of 64 sampled query rows.  The
+// sample is the strided row set {floor(r * S / 512) : r < 512} of each head
+// (the reference draws 512 rows with a seeded randperm; any fixed spread
+// sample estimates the same population spread).  Scores use the fp16 q/k
+// the attention consumes, accumulated in fp32.
+__global__ void __launch_bounds__(256) poly_guard_kernel(PolyParams p) {
+  __shared__ float qs[64][65];
+  __shared__ float ks[64][65];
+  __shared__ double dred[2][8];
+  __shared__ float mred[8];
+  const int bh = blockIdx.y;
+  const __half* qb = p.q + (size_t)bh * p.S * 64;
+  const __half* kb = p.k + (size_t)bh * p.S * 64;
+  for (int i = threadIdx.x; i < 64 * 64; i += blockDim.x) {
+    const int r = i >> 6, c = i & 63;
+    const long long row = (long long)(blockIdx.x * 64 + r) * p.S / kPolySample;
+    qs[r][c] = __half2float(qb[row * 64 + c]);
+  }
+  const int qi = threadIdx.x >> 2;  // query row of this thread
+  const int k0 = threadIdx.x & 3;   // keys k0, k0+4, ... of each tile
+  double sum = 0.0, sumsq = 0.0;
+  float mx = 0.0f;
+  for (int kt = 0; kt < kPolySample / 64; ++kt) {
+    __syncthreads();
+    for (int i = threadIdx.x; i < 64 * 64; i += blockDim.x) {
+      const int r = i >> 6, c = i & 63;
+      const long long row = (long long)(kt * 64 + r) * p.S / kPolySample;
+      ks[r][c] = __half2float(kb[row * 64 + c]);
+    }
+    __syncthreads();
+    float s_loc = 0.f, s2_loc = 0.f;
+    for (int kk = k0; kk < 64; kk += 4) {
+      float dot = 0.f;
+#pragma unroll
+      for (int e = 0; e < 64; ++e) dot = fmaf(qs[qi][e], ks[kk][e], dot);
+      dot *= p.scale;
+      s_loc += dot;
+      s2_loc += dot * dot;
+      mx = fmaxf(mx, fabsf(dot));
+    }
+    sum += s_loc;
+    sumsq += s2_loc;
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    sumsq += __shfl_xor_sync(0xffffffffu, sumsq, o);
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  }
+  const int w = threadIdx.x >> 5;
+  if ((threadIdx.x & 31) == 0) { dred[0][w] = sum; dred[1][w] = sumsq; mred[w] = mx; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double s = 0, s2 = 0;
+    float m = 0;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) { s += dred[0][i]; s2 += dred[1][i]; m = fmaxf(m, mred[i]); }
+    atomicAdd(&p.ctl->sum, s);
+    atomicAdd(&p.ctl->sumsq, s2);
+    // non-negative doubles order like their bit patterns
+    atomicMax(reinterpret_cast<unsigned long long*>(&p.ctl->maxv), (unsigned long long)__double_as_longlong((double)m));
+  }
+}
+
+// Single thread: sigma (unbiased std like torch.std), admission, coefficients.
+__global__ void poly_guard_finalize(PolyParams p) {
+  PolyCtl* c = p.ctl;
+  const double n = (double)p.B * p.H * kPolySample * kPolySample;
+  const double mean = c->sum / n;
+  const double var = (c->sumsq - n * mean * mean) / (n - 1.0);
+  const float sigma = (float)sqrt(var > 0 ? var : 0.0);
+  const float mx = (float)c->maxv;
+  bool unpadded = true;
+  for (int b = 0; b < p.B; ++b) unpadded = unpadded && (p.lengths[b] == p.S);
+  const bool ok = isfinite(sigma) && isfinite(mx) && sigma > 0.f && sigma <= kPolySigmaCeiling &&
+                  mx <= kPolyMaxScore && unpadded;
+  const float g = expf(0.5f * sigma * sigma);
+  c->c0 = g * fmaxf(1.0f - 0.5f * sigma * sigma, 1e-3f);
+  c->c1 = g;
+  c->c2 = 0.5f * g;
+  c->sigma = sigma;
+  c->max_abs = mx;
+  c->admit = ok ? 1 : 0;
+}
+
+// ------------------------------------------------------------------ feature tiles
+// A feature tile is [128 token rows x 128 features] fp16 stored as two
+// 64-feature atoms of [128 rows x 128 B] with the 128-byte swizzle (16-byte
+// chunk c of row r at c ^ (r & 7)).  The same bytes serve as the K-major A
+// operand of the apply GEMM (M = tokens, K = features) and as the MN-major A
+// operand of the update GEMM (M = features, K = tokens).
+TJ_DEV void load_row64(const uint8_t* tile, int row, float (&x)[64]) {
+  const uint8_t* base = tile + row * 128;
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    const uint4 w = *reinterpret_cast<const uint4*>(base + ((c ^ (row & 7)) << 4));
+    const __half2* h = reinterpret_cast<const __half2*>(&w);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __half22float2(h[e]);
+      x[c * 8 + 2 * e] = f.x;
+      x[c * 8 + 2 * e + 1] = f.y;
+    }
+  }
+}
+
+// Elements (i, i+1) (i even) of a row of a [128 x 64] fp16 tile (128B swizzle).
+TJ_DEV float2 load_pair(const uint8_t* tile, int row, int i) {
+  const uint8_t* a = tile + row * 128 + (((i >> 3) ^ (row & 7)) << 4) + (i & 7) * 2;
+  return __half22float2(*reinterpret_cast<const __half2*>(a));
+}
+
+// One atom row: feature j = coef * x[j] (j = 0..63).
+TJ_DEV void store_atom_row(uint8_t* atom, int row, float coef, const float (&x)[64]) {
+  uint8_t* base = atom + row * 128;
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    uint4 w;
+    w.x = pack_half2(coef * x[c * 8 + 0], coef * x[c * 8 + 1]);
+    w.y = pack_half2(coef * x[c * 8 + 2], coef * x[c * 8 + 3]);
+    w.z = pack_half2(coef * x[c * 8 + 4], coef * x[c * 8 + 5]);
+    w.w = pack_half2(coef * x[c * 8 + 6], coef * x[c * 8 + 7]);
+    *reinterpret_cast<uint4*>(base + ((c ^ (row & 7)) << 4)) = w;
+  }
+}
+// One atom row holding a single constant in feature 0 (the phi0 slot), zeros elsewhere.
+TJ_DEV void store_const_row(uint8_t* atom, int row, float c0) {
+  uint8_t* base = atom + row * 128;
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    uint4 w = make_uint4(0u, 0u, 0u, 0u);
+    if (c == 0) w.x = pack_half2(c0, 0.f);
+    *reinterpret_cast<uint4*>(base + ((c ^ (row & 7)) << 4)) = w;
+  }
+}
+
+// Writes feature block fb of this token row (x = the row, xi = elements
+// 2fb and 2fb+1 of it).  quad/lin/cst are the phi2, phi1 and phi0
+// coefficients (key side: scale, sqrt(scale), 1; query side folded with
+// c2, c1, c0).
+TJ_DEV void store_feature_block(uint8_t* tile, int row, int fb, const float (&x)[64], float2 xi, float quad,
+                                float lin, float cst) {
+  if (fb < 32) {
+    store_atom_row(tile, row, quad * xi.x, x);
+    store_atom_row(tile + 16384, row, quad * xi.y, x);
+  } else {
+    store_atom_row(tile, row, lin, x);
+    store_const_row(tile + 16384, row, cst);
+  }
+}
+
+// The constant B operand [N=16 rows x K=128] (K-major, 128B swizzle): row 0 all ones.
+TJ_DEV void init_ones_tile(uint8_t* ones, int tid, int nthreads) {
+  for (int i = tid; i < 4096 / 16; i += nthreads) {  // 2 atoms x 16 rows x 8 chunks
+    const int row = (i >> 3) & 15;
+    const uint32_t one2 = row == 0 ? 0x3C003C00u : 0u;  // two fp16 1.0
+    *reinterpret_cast<uint4*>(ones + i * 16) = make_uint4(one2, one2, one2, one2);
+  }
+}
+
+// Chunk c's delta (TMEM buffer c & 1) -> running fp32 state (registers) ->
+// fp16 MEAN snapshot for chunk c+1 (row frow of feature block fb).
+TJ_DEV bool update_drain(const PolyParams& p, uint32_t tmem, int quarter, int frow, int fb, int bh, int c,
+                         int n_chunks, uint64_t* d_full, uint64_t* d_empty, float (&state)[65]) {
+  const int db = c & 1;
+  if (!mbar_wait(d_full + db, (c >> 1) & 1, p.err, kErrPolyWait)) return false;
+  tc_fence_after();
+  uint32_t r[32];
+  const uint32_t a = tmem + ((uint32_t)(quarter * 32) << 16) + db * 128;
+#pragma unroll
+  for (int part = 0; part < 3; ++part) {
+    tmem_ld32(a + part * 32, r);
+    tmem_ld_wait();
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (part * 32 + i < 65) state[part * 32 + i] += __uint_as_float(r[i]);
+  }
+  tc_fence_before();
+  mbar_arrive(d_empty + db);
+  const int cn = c + 1;
+  if (cn >= p.prefix_chunks && cn < n_chunks) {
+    const float inv = 1.0f / (float)(cn * kPolyChunk);
+    __half* dst = p.snap +
+                  (((size_t)bh * (n_chunks - p.prefix_chunks) + (cn - p.prefix_chunks)) * kPolyN) * kPolyFeat +
+                  (size_t)fb * 128 + frow;
+#pragma unroll
+    for (int n = 0; n < kPolyN; ++n) dst[(size_t)n * kPolyFeat] = __float2half_rn(n < 65 ? state[n] * inv : 0.f);
+  }
+  return true;
+}
+
+// ------------------------------------------------------------------ update
+constexpr int kUpdStages = 4;     // K/V sub-chunk ring
+constexpr int kUpdPhiBufs = 2;
+constexpr int kUpdSmem = kUpdStages * 32768 + kUpdPhiBufs * 32768 + 4096 + 1024 + 256;
+
+__global__ void __launch_bounds__(192, 1)
+    poly_update_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                       const PolyParams p) {
+  if (p.ctl->admit == 0 || error_raised(p.err)) return;
+  const int fb = blockIdx.x;
+  const int bh = blockIdx.y;
+  const int n_chunks = p.S / kPolyChunk;
+  const int n_sub = (n_chunks - 1) * 4;  // the last chunk's keys feed no later query
+  if (n_sub <= 0) return;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sKV = smem;                                  // stage: K 16 KB | V 16 KB
+  uint8_t* sPhi = sKV + kUpdStages * 32768;             // [2][32 KB]
+  uint8_t* sOnes = sPhi + kUpdPhiBufs * 32768;          // 4 KB
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sOnes + 4096);
+  uint64_t* kv_full = bars;
+  uint64_t* kv_empty = kv_full + kUpdStages;
+  uint64_t* phi_full = kv_empty + kUpdStages;
+  uint64_t* phi_empty = phi_full + kUpdPhiBufs;
+  uint64_t* d_full = phi_empty + kUpdPhiBufs;  // [2] chunk delta ready
+  uint64_t* d_empty = d_full + 2;              // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(d_empty + 2);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kUpdStages; ++i) { mbar_init(kv_full + i, 1); mbar_init(kv_empty + i, 129); }
+    for (int i = 0; i < kUpdPhiBufs; ++i) { mbar_init(phi_full + i, 128); mbar_init(phi_empty + i, 1); }
+    for (int i = 0; i < 2; ++i) { mbar_init(d_full + i, 1); mbar_init(d_empty + i, 128); }
+    fence_mbar_init();
+  }
+  if (warp >= 2) init_ones_tile(sOnes, threadIdx.x - 64, 128);
+  if (warp == 1) { tmem_alloc(tmem_slot, 256); tmem_relinquish(); }
+  fence_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int row0 = bh * p.S;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      for (int u = 0; u < n_sub; ++u) {
+        const int st = u % kUpdStages;
+        if (!mbar_wait(kv_empty + st, ((u / kUpdStages) & 1) ^ 1, p.err, kErrPolyWait)) break;
+        mbar_expect_tx(kv_full + st, 32768);
+        tma_load_2d(sKV + st * 32768, &tmK, kv_full + st, 0, row0 + u * 128);
+        tma_load_2d(sKV + st * 32768 + 16384, &tmV, kv_full + st, 0, row0 + u * 128);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc_v = idesc_f16_f32(128, 64, true, true);     // A MN-major, B MN-major
+      constexpr uint32_t idesc_1 = idesc_f16_f32(128, 16, true, false);    // A MN-major, B K-major
+      const uint32_t ones = smem_u32(sOnes);
+      bool ok = true;
+      for (int u = 0; u < n_sub && ok; ++u) {
+        const int st = u % kUpdStages, pb = u % kUpdPhiBufs;
+        const int c = u >> 2, db = c & 1;
+        if ((u & 3) == 0 && !mbar_wait(d_empty + db, ((c >> 1) & 1) ^ 1, p.err, kErrPolyWait)) { ok = false; break; }
+        if (!mbar_wait(kv_full + st, (u / kUpdStages) & 1, p.err, kErrPolyWait)) { ok = false; break; }
+        if (!mbar_wait(phi_full + pb, (u / kUpdPhiBufs) & 1, p.err, kErrPolyWait)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t phi = smem_u32(sPhi + pb * 32768);
+        const uint32_t vv = smem_u32(sKV + st * 32768 + 16384);
+        const uint32_t d = tmem + db * 128;
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {  // K = 128 tokens, 16 per MMA
+          const uint64_t ad = smem_desc(phi + ks * 2048, 16384, 1024, 128);
+          const uint64_t bv = smem_desc(vv + ks * 2048, 8192, 1024, 128);
+          const uint64_t b1 = smem_desc(ones + (ks >> 2) * 2048 + (ks & 3) * 32, 16, 1024, 128);
+          umma_f16_ss(d, ad, bv, idesc_v, ((u & 3) | ks) != 0);
+          umma_f16_ss(d + 64, ad, b1, idesc_1, ((u & 3) | ks) != 0);
+        }
+        umma_commit(kv_empty + st);
+        umma_commit(phi_empty + pb);
+        if ((u & 3) == 3) umma_commit(d_full + db);
+      }
+    }
+  } else {
+    // ---------------------------------------------------- phi_k producer + state epilogue
+    const int gt = threadIdx.x - 64;      // token row for generation
+    const int quarter = warp & 3;         // TMEM lanes of this warp (feature rows)
+    const int frow = quarter * 32 + lane; // feature row of this thread in the epilogue
+    const float rs = sqrtf(p.scale);
+    float state[65];
+#pragma unroll
+    for (int n = 0; n < 65; ++n) state[n] = 0.f;
+    bool ok = true;
+    // snapshots of chunks before the first delta that matters are all zero except chunk 0 (never used)
+    for (int u = 0; u < n_sub && ok; ++u) {
+      const int st = u % kUpdStages, pb = u % kUpdPhiBufs;
+      if (!mbar_wait(kv_full + st, (u / kUpdStages) & 1, p.err, kErrPolyWait)) { ok = false; break; }
+      if (!mbar_wait(phi_empty + pb, ((u / kUpdPhiBufs) & 1) ^ 1, p.err, kErrPolyWait)) { ok = false; break; }
+      float x[64];
+      load_row64(sKV + st * 32768, gt, x);
+      const float2 xi = fb < 32 ? load_pair(sKV + st * 32768, gt, 2 * fb) : make_float2(0.f, 0.f);
+      store_feature_block(sPhi + pb * 32768, gt, fb, x, xi, p.scale, rs, 1.0f);
+      fence_async_smem();
+      mbar_arrive(phi_full + pb);
+      mbar_arrive(kv_empty + st);  // K rows read (the MMA commit covers V)
+      // drain the previous chunk's delta once this chunk's first sub-chunk is queued
+      if ((u & 3) == 0 && u >= 4 &&
+          !update_drain(p, tmem, quarter, frow, fb, bh, (u >> 2) - 1, n_chunks, d_full, d_empty, state)) {
+        ok = false;
+        break;
+      }
+    }
+    if (ok) update_drain(p, tmem, quarter, frow, fb, bh, (n_sub >> 2) - 1, n_chunks, d_full, d_empty, state);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, 256);
+}
+
+// ------------------------------------------------------------------ apply
+constexpr int kAppSnapStages = 3;  // snapshot K-block ring (2 x [80 x 64] fp16 = 20 KB)
+constexpr int kAppSnapBytes = 20480;
+constexpr int kAppPhiBufs = 2;
+constexpr int kAppSmem = 16384 /*Q*/ + 2 * 32768 /*diag K,V ring*/ + kAppSnapStages * kAppSnapBytes +
+                         kAppPhiBufs * 32768 + 4096 /*ones*/ + 1024 + 256;
+
+__global__ void __launch_bounds__(192, 1)
+    poly_apply_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                      const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmSnap,
+                      const PolyParams p) {
+  if (p.ctl->admit == 0 || error_raised(p.err)) return;
+  const int bh = blockIdx.y;
+  const int b = bh / p.H, h = bh - (bh / p.H) * p.H;
+  const int n_chunks = p.S / kPolyChunk;
+  const int u = p.prefix_chunks * 4 + (int)blockIdx.x;  // global 128-query block
+  const int c = u >> 2;                                 // its chunk
+  const int sblk = u & 3;                               // its block inside the chunk
+  const int n_diag = sblk + 1;                          // key blocks of the diagonal chunk
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sKV = sQ + 16384;                              // [2][K 16 KB | V 16 KB] -> 2 x 32 KB
+  uint8_t* sSnap = sKV + 2 * 32768;
+  uint8_t* sPhi = sSnap + kAppSnapStages * kAppSnapBytes;
+  uint8_t* sOnes = sPhi + kAppPhiBufs * 32768;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sOnes + 4096);
+  uint64_t* q_full = bars;
+  uint64_t* sn_full = q_full + 1;
+  uint64_t* sn_empty = sn_full + kAppSnapStages;
+  uint64_t* phi_full = sn_empty + kAppSnapStages;
+  uint64_t* phi_empty = phi_full + kAppPhiBufs;
+  uint64_t* kv_full = phi_empty + kAppPhiBufs;  // [2]
+  uint64_t* kv_empty = kv_full + 2;             // [2]
+  uint64_t* s_full = kv_empty + 2;
+  uint64_t* p_full = s_full + 1;
+  uint64_t* pv_done = p_full + 1;
+  uint64_t* inter_done = pv_done + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(inter_done + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < kAppSnapStages; ++i) { mbar_init(sn_full + i, 1); mbar_init(sn_empty + i, 1); }
+    for (int i = 0; i < kAppPhiBufs; ++i) { mbar_init(phi_full + i, 128); mbar_init(phi_empty + i, 1); }
+    for (int i = 0; i < 2; ++i) { mbar_init(kv_full + i, 1); mbar_init(kv_empty + i, 1); }
+    mbar_init(s_full, 1);
+    mbar_init(p_full, 128);
+    mbar_init(pv_done, 1);
+    mbar_init(inter_done, 1);
+    fence_mbar_init();
+  }
+  if (warp >= 2) init_ones_tile(sOnes, threadIdx.x - 64, 128);
+  if (warp == 1) { tmem_alloc(tmem_slot, 512); tmem_relinquish(); }
+  fence_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  // TMEM: inter acc [0, 80) | diag acc [128, 208) | S [256, 384) | P [384, 448)
+  const uint32_t t_inter = tmem, t_diag = tmem + 128, t_s = tmem + 256, t_p = tmem + 384;
+  const int row0 = bh * p.S;
+  const int snap_row0 = (bh * (n_chunks - p.prefix_chunks) + (c - p.prefix_chunks)) * kPolyN;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmSnap);
+      mbar_expect_tx(q_full, 16384);
+      tma_load_2d(sQ, &tmQ, q_full, 0, row0 + u * 128);
+      for (int kb = 0; kb < kPolyFeatBlocks; ++kb) {
+        const int st = kb % kAppSnapStages;
+        if (!mbar_wait(sn_empty + st, ((kb / kAppSnapStages) & 1) ^ 1, p.err, kErrPolyWait)) return;
+        mbar_expect_tx(sn_full + st, kAppSnapBytes);
+        tma_load_2d(sSnap + st * kAppSnapBytes, &tmSnap, sn_full + st, kb * 128, snap_row0);
+        tma_load_2d(sSnap + st * kAppSnapBytes + 10240, &tmSnap, sn_full + st, kb * 128 + 64, snap_row0);
+      }
+      for (int j = 0; j < n_diag; ++j) {
+        const int st = j & 1;
+        if (!mbar_wait(kv_empty + st, ((j >> 1) & 1) ^ 1, p.err, kErrPolyWait)) return;
+        mbar_expect_tx(kv_full + st, 32768);
+        tma_load_2d(sKV + st * 32768, &tmK, kv_full + st, 0, row0 + (c * 4 + j) * 128);
+        tma_load_2d(sKV + st * 32768 + 16384, &tmV, kv_full + st, 0, row0 + (c * 4 + j) * 128);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc_inter = idesc_f16_f32(128, kPolyN, false, false);
+      constexpr uint32_t idesc_s = idesc_f16_f32(128, 128, false, false);
+      constexpr uint32_t idesc_pv = idesc_f16_f32(128, 64, false, true);
+      constexpr uint32_t idesc_p1 = idesc_f16_f32(128, 16, false, false);
+      const uint32_t ones = smem_u32(sOnes);
+      bool ok = true;
+      // phase 1: inter = phi_q(q) @ S_c over 33 feature blocks
+      for (int kb = 0; kb < kPolyFeatBlocks && ok; ++kb) {
+        const int st = kb % kAppSnapStages, pb = kb % kAppPhiBufs;
+        if (!mbar_wait(sn_full + st, (kb / kAppSnapStages) & 1, p.err, kErrPolyWait)) { ok = false; break; }
+        if (!mbar_wait(phi_full + pb, (kb / kAppPhiBufs) & 1, p.err, kErrPolyWait)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t phi = smem_u32(sPhi + pb * 32768);
+        const uint32_t sn = smem_u32(sSnap + st * kAppSnapBytes);
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {  // K = 128 features
+          const uint64_t ad = smem_desc(phi + (ks >> 2) * 16384 + (ks & 3) * 32, 16, 1024, 128);
+          const uint64_t bd = smem_desc(sn + (ks >> 2) * 10240 + (ks & 3) * 32, 16, 1024, 128);
+          umma_f16_ss(t_inter, ad, bd, idesc_inter, (kb | ks) != 0);
+        }
+        umma_commit(sn_empty + st);
+        umma_commit(phi_empty + pb);
+      }
+      if (ok) umma_commit(inter_done);
+      // phase 2: diagonal block, exact exp
+      if (ok && !mbar_wait(q_full, 0, p.err, kErrPolyWait)) ok = false;
+      const uint32_t qa = smem_u32(sQ);
+      for (int j = 0; j < n_diag && ok; ++j) {
+        const int st = j & 1;
+        if (!mbar_wait(kv_full + st, (j >> 1) & 1, p.err, kErrPolyWait)) { ok = false; break; }
+        if (j > 0 && !mbar_wait(pv_done, (j - 1) & 1, p.err, kErrPolyWait)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t ka = smem_u32(sKV + st * 32768);
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks) {
+          const uint64_t ad = smem_desc(qa + ks * 32, 16, 1024, 128);
+          const uint64_t bd = smem_desc(ka + ks * 32, 16, 1024, 128);
+          umma_f16_ss(t_s, ad, bd, idesc_s, ks != 0);
+        }
+        umma_commit(s_full);
+        if (!mbar_wait(p_full, j & 1, p.err, kErrPolyWait)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t va = ka + 16384;
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+          const uint64_t bv = smem_desc(va + ks * 2048, 8192, 1024, 128);
+          const uint64_t b1 = smem_desc(ones + (ks >> 2) * 2048 + (ks & 3) * 32, 16, 1024, 128);
+          umma_f16_ts(t_diag, t_p + ks * 8, bv, idesc_pv, (j | ks) != 0);
+          umma_f16_ts(t_diag + 64, t_p + ks * 8, b1, idesc_p1, (j | ks) != 0);
+        }
+        umma_commit(pv_done);
+        umma_commit(kv_empty + st);
+      }
+    }
+  } else {
+    // ---------------------------------------------------- phi_q producer, diag exp, epilogue
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;  // query row (TMEM lane) of this thread
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    PolyCtl ctl = *p.ctl;
+    const float rs = sqrtf(p.scale);
+    bool ok = mbar_wait(q_full, 0, p.err, kErrPolyWait);
+    float x[64];
+    if (ok) load_row64(sQ, r, x);
+    for (int kb = 0; kb < kPolyFeatBlocks && ok; ++kb) {
+      const int pb = kb % kAppPhiBufs;
+      if (!mbar_wait(phi_empty + pb, ((kb / kAppPhiBufs) & 1) ^ 1, p.err, kErrPolyWait)) { ok = false; break; }
+      const float2 xi = kb < 32 ? load_pair(sQ, r, 2 * kb) : make_float2(0.f, 0.f);
+      store_feature_block(sPhi + pb * 32768, r, kb, x, xi, ctl.c2 * p.scale, ctl.c1 * rs, ctl.c0);
+      fence_async_smem();
+      mbar_arrive(phi_full + pb);
+    }
+    const int qpos = (sblk * 128) + r;  // query position inside the chunk
+    for (int j = 0; j < n_diag && ok; ++j) {
+      if (!mbar_wait(s_full, j & 1, p.err, kErrPolyWait)) { ok = false; break; }
+      tc_fence_after();
+      uint32_t s[128];
+      tmem_ld32(t_s + lane_off + 0, *reinterpret_cast<uint32_t(*)[32]>(s + 0));
+      tmem_ld32(t_s + lane_off + 32, *reinterpret_cast<uint32_t(*)[32]>(s + 32));
+      tmem_ld32(t_s + lane_off + 64, *reinterpret_cast<uint32_t(*)[32]>(s + 64));
+      tmem_ld32(t_s + lane_off + 96, *reinterpret_cast<uint32_t(*)[32]>(s + 96));
+      tmem_ld_wait();
+      const int lim = (j == sblk) ? r : 127;  // causal inside the chunk
+      const float sl2 = p.scale * 1.4426950408889634f;
+#pragma unroll
+      for (int i = 0; i < 64; ++i) {
+        float v0 = fminf(__uint_as_float(s[2 * i]) * sl2, kPolyMaxScore * 1.4426950408889634f);
+        float v1 = fminf(__uint_as_float(s[2 * i + 1]) * sl2, kPolyMaxScore * 1.4426950408889634f);
+        const float p0 = (2 * i <= lim) ? fast_exp2(v0) : 0.f;
+        const float p1 = (2 * i + 1 <= lim) ? fast_exp2(v1) : 0.f;
+        s[i] = pack_half2(p0, p1);
+      }
+      tmem_st32(t_p + lane_off, *reinterpret_cast<uint32_t(*)[32]>(s));
+      tmem_st32(t_p + lane_off + 32, *reinterpret_cast<uint32_t(*)[32]>(s + 32));
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(p_full);
+      // the next S overwrites the S columns only after PV(j) (waited by the MMA thread)
+    }
+    (void)qpos;
+    if (ok && mbar_wait(inter_done, 0, p.err, kErrPolyWait) &&
+        (n_diag == 0 || mbar_wait(pv_done, (n_diag - 1) & 1, p.err, kErrPolyWait))) {
+      tc_fence_after();
+      const float t_prev = (float)(c * kPolyChunk);
+      uint32_t a0[32], a1[32], d0[32], d1[32];
+      tmem_ld32(t_inter + lane_off, a0);
+      tmem_ld32(t_inter + lane_off + 32, a1);
+      tmem_ld32(t_diag + lane_off, d0);
+      tmem_ld32(t_diag + lane_off + 32, d1);
+      tmem_ld_wait();
+      uint32_t e[32], f[32];
+      tmem_ld32(t_inter + lane_off + 64, e);
+      tmem_ld32(t_diag + lane_off + 64, f);
+      tmem_ld_wait();
+      const float den = t_prev * __uint_as_float(e[0]) + __uint_as_float(f[0]);
+      const float inv = 1.0f / den;
+      const int qrow = u * 128 + r;
+      __half* dst = p.ctx + ((size_t)b * p.S + qrow) * p.d_model + (size_t)h * 64;
+#pragma unroll
+      for (int i = 0; i < 32; i += 8) {
+        uint4 w;
+        w.x = pack_half2((t_prev * __uint_as_float(a0[i]) + __uint_as_float(d0[i])) * inv,
+                         (t_prev * __uint_as_float(a0[i + 1]) + __uint_as_float(d0[i + 1])) * inv);
+        w.y = pack_half2((t_prev * __uint_as_float(a0[i + 2]) + __uint_as_float(d0[i + 2])) * inv,
+                         (t_prev * __uint_as_float(a0[i + 3]) + __uint_as_float(d0[i + 3])) * inv);
+        w.z = pack_half2((t_prev * __uint_as_float(a0[i + 4]) + __uint_as_float(d0[i + 4])) * inv,
+                         (t_prev * __uint_as_float(a0[i + 5]) + __uint_as_float(d0[i + 5])) * inv);
+        w.w = pack_half2((t_prev * __uint_as_float(a0[i + 6]) + __uint_as_float(d0[i + 6])) * inv,
+                         (t_prev * __uint_as_float(a0[i + 7]) + __uint_as_float(d0[i + 7])) * inv);
+        *reinterpret_cast<uint4*>(dst + i) = w;
+        uint4 w2;
+        w2.x = pack_half2((t_prev * __uint_as_float(a1[i]) + __uint_as_float(d1[i])) * inv,
+                          (t_prev * __uint_as_float(a1[i + 1]) + __uint_as_float(d1[i + 1])) * inv);
+        w2.y = pack_half2((t_prev * __uint_as_float(a1[i + 2]) + __uint_as_float(d1[i + 2])) * inv,
+                          (t_prev * __uint_as_float(a1[i + 3]) + __uint_as_float(d1[i + 3])) * inv);
+        w2.z = pack_half2((t_prev * __uint_as_float(a1[i + 4]) + __uint_as_float(d1[i + 4])) * inv,
+                          (t_prev * __uint_as_float(a1[i + 5]) + __uint_as_float(d1[i + 5])) * inv);
+        w2.w = pack_half2((t_prev * __uint_as_float(a1[i + 6]) + __uint_as_float(d1[i + 6])) * inv,
+                          (t_prev * __uint_as_float(a1[i + 7]) + __uint_as_float(d1[i + 7])) * inv);
+        *reinterpret_cast<uint4*>(dst + 32 + i) = w2;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, 512);
+}
+
+}  // namespace tj

@@ -143,11 +143,12 @@ class B200Transformer(nn.Module):
         return self._handle
 
     def _workspace(self, handle: _Handle, batch: int, seq_len: int, device: torch.device) -> torch.Tensor:
-        key = (device, batch, seq_len)
+        route = _ROUTES[self.attention_route]
+        key = (device, batch, seq_len, route)
         ws = self._workspaces.get(key)
         if ws is None:
             nbytes = ctypes.c_size_t()
-            _lib.call("tj_workspace_bytes", handle.ptr, batch, seq_len, ctypes.byref(nbytes))
+            _lib.call("tj_workspace_bytes", handle.ptr, batch, seq_len, route, ctypes.byref(nbytes))
             # zero-filled once: the library only ever writes finite values into it
             ws = torch.zeros(max(int(nbytes.value), 256), dtype=torch.uint8, device=device)
             while len(self._workspaces) >= 4:  # keep the most recent shapes only

@@ -124,3 +124,39 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, info: MaskInfo,
                   int(causal), info.lengths.data_ptr(), _ptr(info.mask), info.general.data_ptr(), err.data_ptr(),
                   _stream(q))
     return ctx
+
+
+class PolyStatus(NamedTuple):
+    admit: bool
+    c0: float
+    c1: float
+    c2: float
+    sigma: float
+    max_abs: float
+
+
+def poly_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, exact_prefix: int = 4096,
+                   err: Optional[torch.Tensor] = None):
+    """Guarded polynomial causal attention (head_dim 64, no padding).
+
+    Returns (ctx fp16 [B*N, H*64], PolyStatus).  Queries below ``exact_prefix``
+    -- or all of them if the device-side guard rejects the route -- come from
+    the exact flash kernel.
+    """
+    _need_cuda(q, k, v)
+    b, h, n, hd = q.shape
+    if hd != 64 or q.dtype != torch.float16 or k.shape != q.shape or v.shape != q.shape:
+        raise ValueError("q, k, v must be fp16 [B, H, N, 64]")
+    nbytes = ctypes.c_size_t()
+    _lib.call("tj_poly_workspace_bytes", b, h, n, exact_prefix, ctypes.byref(nbytes))
+    ws = torch.zeros(int(nbytes.value), dtype=torch.uint8, device=q.device)
+    err = err if err is not None else torch.zeros(1, dtype=torch.int32, device=q.device)
+    lengths = torch.full((b,), n, dtype=torch.int32, device=q.device)
+    ctx = torch.zeros(b * n, h * hd, dtype=torch.float16, device=q.device)
+    with torch.cuda.device(q.device):
+        _lib.call("tj_poly_attention_f16", q.data_ptr(), k.data_ptr(), v.data_ptr(), ctx.data_ptr(),
+                  lengths.data_ptr(), b, h, n, exact_prefix, ws.data_ptr(), ws.numel(), err.data_ptr(), _stream(q))
+    head = ws[:24].cpu()
+    admit = int(head[:4].view(torch.int32).item())
+    c0, c1, c2, sigma, max_abs = (float(v) for v in head[4:24].view(torch.float32))
+    return ctx, PolyStatus(bool(admit), c0, c1, c2, sigma, max_abs)

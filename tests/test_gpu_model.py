@@ -126,6 +126,23 @@ def test_c5_exact_route_full_length_sample():
         assert v.passed, f"{v.failed_elements} failed, max_abs={v.max_abs_error:.3g}"
 
 
+def test_c5_poly_route_full_length_sample():
+    """C5 through the guarded polynomial route (auto-selected at N=262144):
+    sample 0 in full against the bounded-memory FP32 oracle with EXACT
+    attention -- the approximation itself must stay inside the tolerance."""
+    cfg, pr, ls = _shape("C5")
+    oracle, cand = _models(cfg, ls)
+    cand.attention_route = "auto"
+    with torch.inference_mode():
+        x, mask = generate_random_case(cfg, DEV, torch.float32, 1234, pr)
+        got = cand(x, mask)
+        assert cand.device_error() == 0
+        assert torch.isfinite(got).all()
+        ref = linear_memory.linear_memory_forward(oracle, x[:1], mask[:1], q_chunk=256)
+        v = check_outputs(ref, got[:1])
+        assert v.passed, f"{v.failed_elements} failed, max_abs={v.max_abs_error:.3g}"
+
+
 def test_noncausal_and_general_mask():
     cfg = EncoderShape(3, 320, 256, 4, 512, 2, False)
     oracle, cand = _models(cfg, 1.0)

@@ -40,7 +40,7 @@ def test_library_rejects_bad_arguments_without_gpu():
     cfg = _lib.TjConfig(1000, 16, 4096, 1, 1, 1e-5)  # head_dim not supported
     assert lib.tj_model_create(ctypes.byref(cfg), ctypes.byref(out)) in (1, 2)
     size = ctypes.c_size_t()
-    assert lib.tj_workspace_bytes(None, 1, 1, ctypes.byref(size)) == 1
+    assert lib.tj_workspace_bytes(None, 1, 1, 0, ctypes.byref(size)) == 1
 
 
 def test_candidate_contract_validates():
