@@ -48,7 +48,8 @@ typedef enum TjStatus {
   TJ_ERR_UNSUPPORTED = 2,  /* shape outside the kernels' envelope (e.g. head_dim) */
   TJ_ERR_CUDA = 3,         /* CUDA runtime / driver error */
   TJ_ERR_DEVICE = 4,       /* a kernel's bounded wait expired; see tj_device_error */
-  TJ_ERR_NO_DEVICE = 5     /* no sm_100 device is current */
+  TJ_ERR_NO_DEVICE = 5,    /* no sm_100 device is current */
+  TJ_ERR_NCCL = 6          /* NCCL missing, failed or timed out (communicator aborted) */
 } TjStatus;
 
 /* Attention evaluation route for the forward pass. */
@@ -194,6 +195,29 @@ TJ_API int tj_gemm_f16(const void* a, const void* w, const float* bias, int batc
 TJ_API int tj_attention_f16(const void* q, const void* k, const void* v, void* ctx, int batch, int heads, int seq_len,
                      int head_dim, int causal, const int* lengths, const uint8_t* mask, const uint8_t* general,
                      int* err, void* stream);
+
+/* ---- sequence sharding over NCCL (one process per GPU) ----------------- */
+
+typedef struct TjComm TjComm;
+/* 128-byte NCCL unique id, made on one rank and shared with the others by the
+   host (e.g. a torch.distributed broadcast). */
+TJ_API int tj_nccl_unique_id(void* id_out);
+/* Joins the communicator (non-blocking NCCL init polled up to timeout_ms; on
+   expiry the communicator is aborted and TJ_ERR_NCCL returned). */
+TJ_API int tj_comm_create(const void* id, int rank, int world, int timeout_ms, TjComm** out);
+TJ_API int tj_comm_destroy(TjComm* comm);
+TJ_API int tj_workspace_bytes_seqshard(const TjModel* model, const TjComm* comm, int batch, int seq_local, int route,
+                                       size_t* bytes);
+/* Forward of rank r's sequence shard: x/out hold global tokens
+   [r*seq_local, (r+1)*seq_local) of every sample ([B, seq_local, d], FP32),
+   causal, no padding.  Token-local work runs on the shard; attention takes
+   the guarded polynomial route (guard statistics all-reduced so every rank
+   decides alike; each rank's state total all-gathered and folded into its
+   snapshots) or the exact flash route over all-gathered K/V.  Replaces the
+   single-GPU prefix streaming of forward_prefix_chunks
+   (src/implementations/extreme.py:167-204). */
+TJ_API int tj_forward_seqshard(TjModel* model, TjComm* comm, const float* x, float* out, int batch, int seq_local,
+                               int route, void* workspace, size_t workspace_bytes, void* stream);
 
 /* Guarded polynomial causal attention over Q,K,V fp16 [B,H,S,64] with no
    padding (lengths[b] == S), replacing PolyOrFlashSelfAttention.forward +

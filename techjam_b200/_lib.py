@@ -15,7 +15,7 @@ LIB_PATH = Path(__file__).resolve().with_name("libtj.so")
 
 TJ_OK = 0
 STATUS_NAMES = {0: "TJ_OK", 1: "TJ_ERR_INVALID", 2: "TJ_ERR_UNSUPPORTED", 3: "TJ_ERR_CUDA",
-                4: "TJ_ERR_DEVICE", 5: "TJ_ERR_NO_DEVICE"}
+                4: "TJ_ERR_DEVICE", 5: "TJ_ERR_NO_DEVICE", 6: "TJ_ERR_NCCL"}
 ROUTE_EXACT, ROUTE_POLY, ROUTE_AUTO = 0, 1, 2
 EPI_QKV, EPI_GELU, EPI_RESID, EPI_PLAIN16 = 0, 1, 2, 3
 KERNEL_CLASSES = ("prep", "layernorm", "gemm_qkv", "attention", "gemm_out", "gemm_ffn_in", "gemm_ffn_out",
@@ -66,6 +66,12 @@ SIGNATURES = {
     "tj_gemm_f16": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p,
                             c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                             c_void_p]),
+    "tj_nccl_unique_id": (c_int, [c_void_p]),
+    "tj_comm_create": (c_int, [c_void_p, c_int, c_int, c_int, POINTER(c_void_p)]),
+    "tj_comm_destroy": (c_int, [c_void_p]),
+    "tj_workspace_bytes_seqshard": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, POINTER(c_size_t)]),
+    "tj_forward_seqshard": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_size_t,
+                                    c_void_p]),
     "tj_poly_workspace_bytes": (c_int, [c_int, c_int, c_int, c_int, POINTER(c_size_t)]),
     "tj_poly_attention_f16": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int,
                                       c_void_p, c_size_t, c_void_p, c_void_p]),

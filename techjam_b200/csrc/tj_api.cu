@@ -159,9 +159,11 @@ int launch_attn_hd(const void* q, const void* k, const void* v, const tj::AttnPa
   using Cfg = tj::AttnCfg<HD>;
   CUtensorMap tq, tk, tv;
   const uint64_t rows = (uint64_t)B * p.H * p.S;
+  // K/V may hold several sequence shards of kv_shard rows (gathered by NCCL)
+  const uint64_t kv_rows = (uint64_t)B * p.H * (uint64_t)p.kv_shard * (uint64_t)p.kv_shards;
   TJ_CHECK(make_map_f16(&tq, q, rows, HD, 128, Cfg::kAtomCols, Cfg::kSw));
-  TJ_CHECK(make_map_f16(&tk, k, rows, HD, 128, Cfg::kAtomCols, Cfg::kSw));
-  TJ_CHECK(make_map_f16(&tv, v, rows, HD, 128, Cfg::kAtomCols, Cfg::kSw));
+  TJ_CHECK(make_map_f16(&tk, k, kv_rows, HD, 128, Cfg::kAtomCols, Cfg::kSw));
+  TJ_CHECK(make_map_f16(&tv, v, kv_rows, HD, 128, Cfg::kAtomCols, Cfg::kSw));
   auto kern = tj::attn_fwd_kernel<HD>;
   static bool attr_set[64] = {};
   int dev = 0;
@@ -352,6 +354,11 @@ int launch_poly_route(const __half* q, const __half* k, const __half* v, __half*
   pp.prefix_chunks = exact_prefix / tj::kPolyChunk;
   pp.scale = 0.125f;  // 64^-0.5
   pp.err = ap_in.err;
+  pp.S_total = S;
+  pp.t_before = 0.f;
+  pp.total = nullptr;
+  pp.all_chunks = 0;
+  pp.guard_shards = 1;
   const int n_chunks = S / tj::kPolyChunk;
   if (pp.prefix_chunks < 1 || pp.prefix_chunks >= n_chunks || exact_prefix % tj::kPolyChunk)
     return fail(TJ_ERR_UNSUPPORTED, "polynomial route needs 512 <= exact prefix < seq_len, multiple of 512");
@@ -570,6 +577,10 @@ int tj_forward(TjModel* m, const float* x, const uint8_t* mask, float* out, int 
   ap.causal = c.causal ? 1 : 0;
   ap.scale_log2 = (float)(1.0 / std::sqrt((double)hd) * 1.4426950408889634);
   ap.err = m->err;
+  ap.q_pos0 = 0;
+  ap.kv_shard = S;
+  ap.kv_shards = 1;
+  ap.B = B;
 
   const float eps = c.layer_norm_eps;
   const float* resid_in = x;
@@ -689,6 +700,10 @@ int tj_poly_attention_f16(const void* q, const void* k, const void* v, void* ctx
   ap.S = S; ap.H = H; ap.d_model = H * 64; ap.causal = 1;
   ap.scale_log2 = (float)(0.125 * 1.4426950408889634);
   ap.err = err;
+  ap.q_pos0 = 0;
+  ap.kv_shard = S;
+  ap.kv_shards = 1;
+  ap.B = B;
   return launch_poly_route(static_cast<const __half*>(q), static_cast<const __half*>(k),
                            static_cast<const __half*>(v), static_cast<__half*>(ctx), lengths, B, H, S, H * 64,
                            exact_prefix, ctl, snap, nullptr, ap, static_cast<cudaStream_t>(stream));
@@ -780,7 +795,295 @@ int tj_attention_f16(const void* q, const void* k, const void* v, void* ctx, int
   p.S = S; p.H = H; p.d_model = H * hd; p.causal = causal ? 1 : 0;
   p.scale_log2 = (float)(1.0 / std::sqrt((double)hd) * 1.4426950408889634);
   p.err = err;
+  p.q_pos0 = 0;
+  p.kv_shard = S;
+  p.kv_shards = 1;
+  p.B = B;
   return launch_attention(q, k, v, hd, p, B, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"
+
+// ------------------------------------------------------------------ sequence-sharded forward (NCCL)
+#include "tj_nccl.cuh"
+
+struct TjComm {
+  ncclComm_t comm = nullptr;
+  int rank = 0;
+  int world = 1;
+  int timeout_ms = 60000;
+  bool broken = false;
+};
+
+namespace {
+
+int nccl_check(TjComm* c, ncclResult_t r, const char* what) {
+  if (r == ncclInProgress) r = tj::nccl_settle(c->comm, c->timeout_ms);
+  if (r == ncclSuccess) return TJ_OK;
+  c->broken = true;
+  tj::nccl().CommAbort(c->comm);
+  c->comm = nullptr;
+  return fail(TJ_ERR_NCCL, "%s: %s", what,
+              r == ncclInProgress ? "timed out (peer missing?); communicator aborted" : tj::nccl().GetErrorString(r));
+}
+
+struct ShardWorkspace {
+  Workspace base;
+  tj::PolyCtl* ctl;
+  __half* snap;
+  float* total;     // [B*H][80][4224] fp32: this shard's state
+  float* gathered;  // [world][B*H][80][4224]
+  __half* kg;       // [world][B][H][S_loc][64]: every shard's K (exact route)
+  __half* vg;
+};
+
+bool shard_poly_eligible(const TjConfig& c, int S_loc, int world, int route) {
+  if (route == TJ_ROUTE_EXACT || !c.causal || c.d_model / c.num_heads != 64) return false;
+  if (S_loc % tj::kPolyChunk != 0 || S_loc <= kPolyExactPrefix) return false;
+  return route == TJ_ROUTE_POLY || (long long)S_loc * world >= kPolyAutoMinSeq;
+}
+
+size_t carve_shard(const TjConfig& c, int B, int S_loc, int world, int route, uint8_t* base, ShardWorkspace* w) {
+  Workspace bw;
+  size_t off = carve(c, B, S_loc, TJ_ROUTE_EXACT, base, &bw);
+  auto take = [&](size_t bytes) {
+    uint8_t* p = base ? base + off : nullptr;
+    off = align_up(off + bytes, 256);
+    return p;
+  };
+  ShardWorkspace t{};
+  t.base = bw;
+  const size_t BH = (size_t)B * c.num_heads;
+  if (shard_poly_eligible(c, S_loc, world, route)) {
+    const size_t state = BH * tj::kPolyN * tj::kPolyFeat;
+    t.ctl = reinterpret_cast<tj::PolyCtl*>(take(sizeof(tj::PolyCtl)));
+    t.snap = reinterpret_cast<__half*>(take(2 * BH * (S_loc / tj::kPolyChunk) * tj::kPolyN * tj::kPolyFeat));
+    t.total = reinterpret_cast<float*>(take(4 * state));
+    t.gathered = reinterpret_cast<float*>(take(4 * state * world));
+  }
+  const size_t kv = (size_t)B * c.num_heads * S_loc * (c.d_model / c.num_heads);
+  t.kg = reinterpret_cast<__half*>(take(2 * kv * world));
+  t.vg = reinterpret_cast<__half*>(take(2 * kv * world));
+  if (w) *w = t;
+  return off;
+}
+
+__global__ void fill_int_kernel(int* dst, int n, int value) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) dst[i] = value;
+}
+
+// Attention of one layer on a sequence shard: guarded polynomial route with a
+// state exchange, or exact flash over all-gathered K/V.
+int shard_attention(TjModel* m, TjComm* cm, ShardWorkspace& w, int B, int S_loc, int route, const tj::AttnParams& ap0,
+                    cudaStream_t st) {
+  const TjConfig& c = m->cfg;
+  const int H = c.num_heads, hd = c.d_model / H, d = c.d_model;
+  const int world = cm->world, rank = cm->rank;
+  const int S_total = S_loc * world;
+  auto& nc = tj::nccl();
+  bool admit = false;
+  if (w.ctl != nullptr) {
+    tj::PolyParams pp{};
+    pp.q = w.base.q; pp.k = w.base.k; pp.v = w.base.v; pp.ctx = w.base.act; pp.snap = w.snap; pp.ctl = w.ctl;
+    pp.lengths = w.base.lengths;
+    pp.B = B; pp.H = H; pp.S = S_loc; pp.d_model = d;
+    pp.prefix_chunks = rank == 0 ? kPolyExactPrefix / tj::kPolyChunk : 0;
+    pp.scale = 0.125f;
+    pp.err = m->err;
+    pp.S_total = S_total;
+    pp.t_before = (float)rank * (float)S_loc;
+    pp.total = w.total;
+    pp.all_chunks = 1;
+    // guard over every shard's sample, decided identically everywhere
+    TJ_CUDA(cudaMemsetAsync(w.ctl, 0, sizeof(tj::PolyCtl), st));
+    tj::poly_guard_kernel<<<dim3(tj::kPolySample / 64, B * H), 256, 0, st>>>(pp);
+    TJ_CUDA(cudaGetLastError());
+    TJ_CHECK(nccl_check(cm, nc.AllReduce(&w.ctl->sum, &w.ctl->sum, 2, ncclFloat64, ncclSum, cm->comm, st), "guard sum"));
+    TJ_CHECK(nccl_check(cm, nc.AllReduce(&w.ctl->maxv, &w.ctl->maxv, 1, ncclFloat64, ncclMax, cm->comm, st), "guard max"));
+    tj::PolyParams pf = pp;
+    pf.guard_shards = world;  // the pooled sample covers every shard
+    tj::poly_guard_finalize<<<1, 1, 0, st>>>(pf);
+    TJ_CUDA(cudaGetLastError());
+    int flag = 0;
+    TJ_CUDA(cudaMemcpyAsync(&flag, &w.ctl->admit, sizeof(int), cudaMemcpyDeviceToHost, st));
+    TJ_CUDA(cudaStreamSynchronize(st));  // one host sync per layer: the exchange depends on the route
+    admit = flag != 0;
+    if (admit) {
+      const int n_chunks = S_loc / tj::kPolyChunk;
+      const uint64_t rows = (uint64_t)B * H * S_loc;
+      CUtensorMap tq, tk, tv, tsn;
+      TJ_CHECK(make_map_f16(&tq, w.base.q, rows, 64, 128, 64, 128));
+      TJ_CHECK(make_map_f16(&tk, w.base.k, rows, 64, 128, 64, 128));
+      TJ_CHECK(make_map_f16(&tv, w.base.v, rows, 64, 128, 64, 128));
+      const uint64_t snap_rows = (uint64_t)B * H * (n_chunks - pp.prefix_chunks) * tj::kPolyN;
+      TJ_CHECK(make_map_f16(&tsn, w.snap, snap_rows, tj::kPolyFeat, tj::kPolyN, 64, 128));
+      TJ_CUDA(cudaFuncSetAttribute(tj::poly_update_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, tj::kUpdSmem));
+      TJ_CUDA(cudaFuncSetAttribute(tj::poly_apply_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, tj::kAppSmem));
+      TJ_CHECK(timed_launch(m, TJ_K_POLY, 1, st, [&]() -> int {
+        tj::poly_update_kernel<<<dim3(tj::kPolyFeatBlocks, B * H), 192, tj::kUpdSmem, st>>>(tk, tv, pp);
+        TJ_CUDA(cudaGetLastError());
+        return TJ_OK;
+      }));
+      const size_t state = (size_t)B * H * tj::kPolyN * tj::kPolyFeat;
+      TJ_CHECK(nccl_check(cm, nc.AllGather(w.total, w.gathered, state, ncclFloat32, cm->comm, st), "state all-gather"));
+      if (rank > 0) {
+        tj::poly_fixup_kernel<<<1184, 256, 0, st>>>(w.gathered, rank, B * H, w.snap, n_chunks - pp.prefix_chunks,
+                                                     pp.prefix_chunks, pp.t_before);
+        TJ_CUDA(cudaGetLastError());
+      }
+      TJ_CHECK(timed_launch(m, TJ_K_POLY, 1, st, [&]() -> int {
+        tj::poly_apply_kernel<<<dim3((n_chunks - pp.prefix_chunks) * 4, B * H), 192, tj::kAppSmem, st>>>(tq, tk, tv,
+                                                                                                       tsn, pp);
+        TJ_CUDA(cudaGetLastError());
+        return TJ_OK;
+      }));
+      if (rank == 0) {  // exact prefix: every key it needs is local
+        tj::AttnParams ap = ap0;
+        ap.poly_admit = &w.ctl->admit;
+        ap.exact_pairs = kPolyExactPrefix / 256;
+        ap.q_pos0 = 0;
+        ap.kv_shard = S_loc;
+        ap.kv_shards = 1;
+        TJ_CHECK(timed_launch(m, TJ_K_ATTN, 1, st, [&] { return launch_attention(w.base.q, w.base.k, w.base.v, 64,
+                                                                                  ap, B, st); }));
+      }
+      return TJ_OK;
+    }
+  }
+  // exact route: gather every shard's K and V, then local queries at their global positions
+  const size_t kv = (size_t)B * H * S_loc * hd;
+  TJ_CHECK(nccl_check(cm, nc.AllGather(w.base.k, w.kg, kv, ncclFloat16, cm->comm, st), "K all-gather"));
+  TJ_CHECK(nccl_check(cm, nc.AllGather(w.base.v, w.vg, kv, ncclFloat16, cm->comm, st), "V all-gather"));
+  tj::AttnParams ap = ap0;
+  ap.poly_admit = nullptr;
+  ap.q_pos0 = rank * S_loc;
+  ap.kv_shard = S_loc;
+  ap.kv_shards = world;
+  return timed_launch(m, TJ_K_ATTN, 1, st, [&] { return launch_attention(w.base.q, w.kg, w.vg, hd, ap, B, st); });
+}
+
+}  // namespace
+
+extern "C" {
+
+int tj_nccl_unique_id(void* id_out) {
+  if (!id_out) return fail(TJ_ERR_INVALID, "null argument");
+  auto& nc = tj::nccl();
+  if (!nc.ok) return fail(TJ_ERR_NCCL, "NCCL unavailable: %s", nc.why);
+  ncclUniqueId id;
+  const ncclResult_t r = nc.GetUniqueId(&id);
+  if (r != ncclSuccess) return fail(TJ_ERR_NCCL, "ncclGetUniqueId: %s", nc.GetErrorString(r));
+  std::memcpy(id_out, &id, sizeof(id));
+  return TJ_OK;
+}
+
+int tj_comm_create(const void* id, int rank, int world, int timeout_ms, TjComm** out) {
+  if (!id || !out || world <= 0 || rank < 0 || rank >= world) return fail(TJ_ERR_INVALID, "bad communicator arguments");
+  *out = nullptr;
+  auto& nc = tj::nccl();
+  if (!nc.ok) return fail(TJ_ERR_NCCL, "NCCL unavailable: %s", nc.why);
+  ncclUniqueId uid;
+  std::memcpy(&uid, id, sizeof(uid));
+  ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+  cfg.blocking = 0;
+  auto* c = new TjComm();
+  c->rank = rank;
+  c->world = world;
+  c->timeout_ms = timeout_ms > 0 ? timeout_ms : 60000;
+  ncclResult_t r = nc.CommInitRankConfig(&c->comm, world, uid, rank, &cfg);
+  if (r == ncclInProgress || r == ncclSuccess) r = tj::nccl_settle(c->comm, c->timeout_ms);
+  if (r != ncclSuccess) {
+    if (c->comm) nc.CommAbort(c->comm);
+    delete c;
+    return fail(TJ_ERR_NCCL, "ncclCommInitRankConfig: %s",
+                r == ncclInProgress ? "timed out waiting for the other ranks" : nc.GetErrorString(r));
+  }
+  *out = c;
+  return TJ_OK;
+}
+
+int tj_comm_destroy(TjComm* c) {
+  if (!c) return TJ_OK;
+  if (c->comm) {
+    if (c->broken) tj::nccl().CommAbort(c->comm);
+    else tj::nccl().CommDestroy(c->comm);
+  }
+  delete c;
+  return TJ_OK;
+}
+
+int tj_workspace_bytes_seqshard(const TjModel* m, const TjComm* c, int B, int S_loc, int route, size_t* bytes) {
+  if (!m || !c || !bytes || B <= 0 || S_loc <= 0) return fail(TJ_ERR_INVALID, "bad arguments");
+  *bytes = carve_shard(m->cfg, B, S_loc, c->world, route, nullptr, nullptr);
+  return TJ_OK;
+}
+
+int tj_forward_seqshard(TjModel* m, TjComm* cm, const float* x, float* out, int B, int S_loc, int route, void* ws,
+                        size_t ws_bytes, void* stream) {
+  if (!m || !cm || !x || !out || !ws) return fail(TJ_ERR_INVALID, "null argument");
+  if (cm->broken || !cm->comm) return fail(TJ_ERR_NCCL, "communicator is broken");
+  if (B <= 0 || S_loc <= 0 || S_loc % 128) return fail(TJ_ERR_UNSUPPORTED, "seq_len per shard must be a multiple of 128");
+  if (x == out) return fail(TJ_ERR_INVALID, "x and out must not alias");
+  if (!m->cfg.causal) return fail(TJ_ERR_UNSUPPORTED, "sequence sharding needs causal attention");
+  const TjConfig& c = m->cfg;
+  const size_t need = carve_shard(c, B, S_loc, cm->world, route, nullptr, nullptr);
+  if (ws_bytes < need) return fail(TJ_ERR_INVALID, "workspace %zu bytes < required %zu", ws_bytes, need);
+  if ((reinterpret_cast<uintptr_t>(ws) & 255) != 0) return fail(TJ_ERR_INVALID, "workspace not 256-byte aligned");
+  DeviceInfo di;
+  TJ_CHECK(device_info(&di));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  ShardWorkspace w;
+  carve_shard(c, B, S_loc, cm->world, route, static_cast<uint8_t*>(ws), &w);
+  const int d = c.d_model, H = c.num_heads, hd = d / H, F = c.ffn_dim;
+  const int M = B * S_loc;
+  const int S_total = S_loc * cm->world;
+  // unpadded sequences of S_total tokens; every local row is valid
+  TJ_CHECK(timed_launch(m, TJ_K_PREP, 2, st, [&]() -> int {
+    fill_int_kernel<<<(B + 255) / 256, 256, 0, st>>>(w.base.lengths, B, S_total);
+    TJ_CUDA(cudaGetLastError());
+    TJ_CUDA(cudaMemsetAsync(w.base.general, 0, B, st));
+    tj::prep_tiles_kernel<<<1, 1024, 0, st>>>(w.base.lengths, B, S_loc, w.base.tile_list, w.base.n_live,
+                                              w.base.tile_live);
+    TJ_CUDA(cudaGetLastError());
+    return TJ_OK;
+  }));
+  tj::RowValidity rv{w.base.lengths, nullptr, S_loc, (long long)M};
+  tj::GemmParams gp{};
+  gp.M = M; gp.seq = S_loc; gp.lengths = w.base.lengths; gp.mask = nullptr;
+  gp.tile_list = w.base.tile_list; gp.n_live = w.base.n_live;
+  gp.q = w.base.q; gp.k = w.base.k; gp.v = w.base.v;
+  gp.heads = H; gp.head_dim = hd; gp.d_model = d; gp.err = m->err;
+  tj::AttnParams ap{};
+  ap.lengths = w.base.lengths; ap.mask = nullptr; ap.general = w.base.general; ap.ctx = w.base.act;
+  ap.S = S_loc; ap.H = H; ap.d_model = d; ap.causal = 1;
+  ap.scale_log2 = (float)(1.0 / std::sqrt((double)hd) * 1.4426950408889634);
+  ap.err = m->err; ap.B = B; ap.kv_shard = S_loc; ap.kv_shards = 1; ap.q_pos0 = 0;
+  const float eps = c.layer_norm_eps;
+  const float* resid_in = x;
+  for (int l = 0; l < c.num_layers; ++l) {
+    const TjLayerPacked& L = m->layers[l];
+    TJ_CHECK(timed_launch(m, TJ_K_LN, 1, st, [&] {
+      return launch_layernorm(resid_in, L.ln1_g, L.ln1_b, w.base.act, true, false, d, eps, rv, w.base.tile_live, st);
+    }));
+    gp.N = 3 * d; gp.K = d; gp.bias = L.bqkv;
+    TJ_CHECK(timed_launch(m, TJ_K_QKV, 1, st, [&] { return launch_gemm_epi(tj::kEpiQKV, w.base.act, L.wqkv, gp, di.sms, st); }));
+    TJ_CHECK(shard_attention(m, cm, w, B, S_loc, route, ap, st));
+    gp.N = d; gp.K = d; gp.bias = L.bo; gp.out32 = out; gp.resid = resid_in;
+    TJ_CHECK(timed_launch(m, TJ_K_OUT, 1, st, [&] { return launch_gemm_epi(tj::kEpiResid, w.base.act, L.wo, gp, di.sms, st); }));
+    TJ_CHECK(timed_launch(m, TJ_K_LN, 1, st, [&] {
+      return launch_layernorm(out, L.ln2_g, L.ln2_b, w.base.act, true, false, d, eps, rv, w.base.tile_live, st);
+    }));
+    gp.N = F; gp.K = d; gp.bias = L.b1; gp.out16 = w.base.ff;
+    TJ_CHECK(timed_launch(m, TJ_K_FFN_IN, 1, st, [&] { return launch_gemm_epi(tj::kEpiGelu, w.base.act, L.w1, gp, di.sms, st); }));
+    gp.N = d; gp.K = F; gp.bias = L.b2; gp.out32 = out; gp.resid = out;
+    TJ_CHECK(timed_launch(m, TJ_K_FFN_OUT, 1, st, [&] { return launch_gemm_epi(tj::kEpiResid, w.base.ff, L.w2, gp, di.sms, st); }));
+    resid_in = out;
+  }
+  TJ_CHECK(timed_launch(m, TJ_K_LN_FINAL, 1, st, [&] {
+    return launch_layernorm(out, m->final_g, m->final_b, out, false, true, d, eps, rv, w.base.tile_live, st);
+  }));
+  return TJ_OK;
 }
 
 }  // extern "C"

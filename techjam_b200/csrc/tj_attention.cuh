@@ -41,6 +41,14 @@ struct AttnParams {
   // (the exact prefix) are computed here; null = every query.
   const int* poly_admit;
   int exact_pairs;
+  // Sequence sharding: local query row 0 sits at global position q_pos0 and
+  // K/V hold kv_shard rows per (shard, b, h): the key at global position pos
+  // is row ((pos / kv_shard * B + b) * H + h) * kv_shard + pos % kv_shard.
+  // Unsharded: q_pos0 = 0, kv_shard = S.
+  int q_pos0;
+  int kv_shard;
+  int kv_shards;  // shards present in K/V (1 unless sharded)
+  int B;
 };
 
 template <int HD>
@@ -77,16 +85,17 @@ __global__ void __launch_bounds__(320, 1)
   const int h = bh - b * p.H;
   const int n_pairs = gridDim.x;
   const int pair = p.causal ? (n_pairs - 1 - (int)blockIdx.x) : (int)blockIdx.x;
-  const int len = __ldg(p.lengths + b);
-  const int q0 = 2 * pair;
-  if (q0 * 128 >= len) return;
+  const int len = __ldg(p.lengths + b);  // valid keys (global positions)
+  const int q0 = 2 * pair;               // local query tile of warpgroup 0
+  const int qg0 = p.q_pos0 / 128 + q0;   // its global tile
+  if (qg0 * 128 >= len || q0 * 128 >= p.S) return;
   if (error_raised(p.err)) return;
   if (p.poly_admit != nullptr && pair >= p.exact_pairs && *reinterpret_cast<const volatile int*>(p.poly_admit) != 0)
     return;
-  const bool has1 = (q0 + 1) * 128 < len;
+  const bool has1 = (qg0 + 1) * 128 < len && (q0 + 1) * 128 < p.S;
   const int kv_all = (len + 127) / 128;
-  const int nkv0 = p.causal ? q0 + 1 : kv_all;
-  const int nkv1 = has1 ? (p.causal ? q0 + 2 : kv_all) : 0;
+  const int nkv0 = p.causal ? qg0 + 1 : kv_all;
+  const int nkv1 = has1 ? (p.causal ? qg0 + 2 : kv_all) : 0;
   const int n_kv = nkv0 > nkv1 ? nkv0 : nkv1;
   const bool general = p.mask != nullptr && __ldg(p.general + b) != 0;
 
@@ -127,7 +136,12 @@ __global__ void __launch_bounds__(320, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const int row0 = bh * p.S;  // first row of this (b, h) in the [B*H*S, HD] views
+  const int row0 = bh * p.S;  // first Q row of this (b, h) in the [B*H*S, HD] view
+  auto kv_row = [&](int j) {  // first K/V row of key tile j (global positions j*128 ..)
+    const int pos = j * 128;
+    const int shard = pos / p.kv_shard;
+    return ((shard * p.B + b) * p.H + h) * p.kv_shard + (pos - shard * p.kv_shard);
+  };
 
   if (warp == 8) {
     if (lane == 0) {
@@ -149,8 +163,8 @@ __global__ void __launch_bounds__(320, 1)
         mbar_expect_tx(kv_full + st, 2 * Cfg::kTile);
 #pragma unroll
         for (int a = 0; a < Cfg::kAtoms; ++a) {
-          tma_load_2d(sk + a * Cfg::kAtomBytes, &tmK, kv_full + st, a * Cfg::kAtomCols, row0 + j * 128);
-          tma_load_2d(sv + a * Cfg::kAtomBytes, &tmV, kv_full + st, a * Cfg::kAtomCols, row0 + j * 128);
+          tma_load_2d(sk + a * Cfg::kAtomBytes, &tmK, kv_full + st, a * Cfg::kAtomCols, kv_row(j));
+          tma_load_2d(sv + a * Cfg::kAtomBytes, &tmV, kv_full + st, a * Cfg::kAtomCols, kv_row(j));
         }
       }
     }
@@ -265,7 +279,7 @@ __global__ void __launch_bounds__(320, 1)
         mbar_arrive(s_free + t);  // S_t may now be overwritten by S_t(j+1)
       }
       const int kbase = j * 128;
-      const bool diag = p.causal && j == qt;
+      const bool diag = p.causal && j == qg0 + t;
       const bool tail = kbase + 128 > len;
       if (diag || tail || general) {
         const int lim_causal = diag ? r : 127;           // keys with col > lim are in the future

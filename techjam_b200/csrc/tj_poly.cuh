@@ -60,9 +60,18 @@ struct PolyParams {
   PolyCtl* ctl;
   const int* lengths;
   int B, H, S, d_model;
-  int prefix_chunks;  // exact prefix / 512
+  int prefix_chunks;  // exact prefix / 512 (0 on sequence shards after the first)
   float scale;        // head_dim^-0.5
   int* err;
+  // Sequence sharding (unsharded: S_total = S, t_before = 0, total = null,
+  // all_chunks = 0): this shard holds global tokens [t_before, t_before + S)
+  // of sequences S_total long; the update also runs over the last local
+  // chunk and writes the shard's total state (fp32 [B*H][80][4224]).
+  int S_total;
+  float t_before;
+  float* total;
+  int all_chunks;
+  int guard_shards;  // shards whose guard samples were pooled (all-reduced) before finalize
 };
 
 // ------------------------------------------------------------------ guard
@@ -131,13 +140,13 @@ __global__ void __launch_bounds__(256) poly_guard_kernel(PolyParams p) {
 // Single thread: sigma (unbiased std like torch.std), admission, coefficients.
 __global__ void poly_guard_finalize(PolyParams p) {
   PolyCtl* c = p.ctl;
-  const double n = (double)p.B * p.H * kPolySample * kPolySample;
+  const double n = (double)p.B * p.H * (p.guard_shards > 0 ? p.guard_shards : 1) * kPolySample * kPolySample;
   const double mean = c->sum / n;
   const double var = (c->sumsq - n * mean * mean) / (n - 1.0);
   const float sigma = (float)sqrt(var > 0 ? var : 0.0);
   const float mx = (float)c->maxv;
   bool unpadded = true;
-  for (int b = 0; b < p.B; ++b) unpadded = unpadded && (p.lengths[b] == p.S);
+  for (int b = 0; b < p.B; ++b) unpadded = unpadded && (p.lengths[b] == p.S_total);
   const bool ok = isfinite(sigma) && isfinite(mx) && sigma > 0.f && sigma <= kPolySigmaCeiling &&
                   mx <= kPolyMaxScore && unpadded;
   const float g = expf(0.5f * sigma * sigma);
@@ -244,6 +253,11 @@ TJ_DEV bool update_drain(const PolyParams& p, uint32_t tmem, int quarter, int fr
   tc_fence_before();
   mbar_arrive(d_empty + db);
   const int cn = c + 1;
+  if (p.total != nullptr && cn == n_chunks) {  // the shard's total state, fp32
+    float* dst = p.total + ((size_t)bh * kPolyN) * kPolyFeat + (size_t)fb * 128 + frow;
+#pragma unroll
+    for (int n = 0; n < kPolyN; ++n) dst[(size_t)n * kPolyFeat] = n < 65 ? state[n] : 0.f;
+  }
   if (cn >= p.prefix_chunks && cn < n_chunks) {
     const float inv = 1.0f / (float)(cn * kPolyChunk);
     __half* dst = p.snap +
@@ -267,7 +281,8 @@ __global__ void __launch_bounds__(192, 1)
   const int fb = blockIdx.x;
   const int bh = blockIdx.y;
   const int n_chunks = p.S / kPolyChunk;
-  const int n_sub = (n_chunks - 1) * 4;  // the last chunk's keys feed no later query
+  // the last chunk's keys feed no later query of this shard (only later shards)
+  const int n_sub = (p.all_chunks ? n_chunks : n_chunks - 1) * 4;
   if (n_sub <= 0) return;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -564,7 +579,7 @@ __global__ void __launch_bounds__(192, 1)
     if (ok && mbar_wait(inter_done, 0, p.err, kErrPolyWait) &&
         (n_diag == 0 || mbar_wait(pv_done, (n_diag - 1) & 1, p.err, kErrPolyWait))) {
       tc_fence_after();
-      const float t_prev = (float)(c * kPolyChunk);
+      const float t_prev = p.t_before + (float)(c * kPolyChunk);
       uint32_t a0[32], a1[32], d0[32], d1[32];
       tmem_ld32(t_inter + lane_off, a0);
       tmem_ld32(t_inter + lane_off + 32, a1);
@@ -608,6 +623,27 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   tc_fence_after();
   if (warp == 1) tmem_dealloc(tmem, 512);
+}
+
+// ------------------------------------------------------------------ shard fix-up
+// Sequence sharding: fold the state of all earlier shards into this shard's
+// snapshots.  gathered = every shard's total state [world][B*H][80][4224]
+// fp32; local snapshot c holds the mean over this shard's first 512c tokens;
+// afterwards it holds the mean over all tokens before its chunk.
+__global__ void poly_fixup_kernel(const float* __restrict__ gathered, int rank, int BH, __half* __restrict__ snap,
+                                  int n_snap, int prefix_chunks, float t_before) {
+  const size_t per = (size_t)kPolyN * kPolyFeat;
+  const size_t total = (size_t)BH * per;
+  for (size_t e = (size_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (size_t)gridDim.x * blockDim.x) {
+    float before = 0.f;
+    for (int r = 0; r < rank; ++r) before += gathered[(size_t)r * total + e];
+    const size_t bh = e / per, rem = e - bh * per;
+    for (int i = 0; i < n_snap; ++i) {
+      __half* sp = snap + (bh * n_snap + i) * per + rem;
+      const float t_loc = (float)((prefix_chunks + i) * kPolyChunk);
+      *sp = __float2half_rn((__half2float(*sp) * t_loc + before) / (t_loc + t_before));
+    }
+  }
 }
 
 }  // namespace tj

@@ -1,0 +1,68 @@
+"""Host logic of multi-GPU sharding, run as two gloo ranks on the CPU."""
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from techjam_b200.harness import CONFIGS, generate_random_case, valid_lengths
+from techjam_b200.sharding import sample_cost, shard_samples, token_range
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank, world, port, results):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        out = {}
+        for name in ("C2", "C3"):
+            wl = CONFIGS[name]
+            cfg = wl.config
+            _, mask = generate_random_case(cfg, torch.device("cpu"), torch.float32, 101234, wl.padding_ratio)
+            lengths = valid_lengths(mask, cfg.batch_size, cfg.seq_len)
+            mine = shard_samples(lengths, world, rank, cfg.d_model, cfg.ffn_dim)
+            gathered = [None] * world
+            dist.all_gather_object(gathered, mine)
+            out[name] = (gathered, lengths)
+        rng = token_range(262144, world, rank)
+        spans = [None] * world
+        dist.all_gather_object(spans, (rng.start, rng.stop))
+        out["C5"] = spans
+        if rank == 0:
+            results.put(out)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_rank_sharding_partitions_and_balances():
+    ctx = mp.get_context("spawn")
+    results = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, results)) for r in range(2)]
+    for p in procs:
+        p.start()
+    out = results.get(timeout=120)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for name in ("C2", "C3"):
+        gathered, lengths = out[name]
+        flat = sorted(i for part in gathered for i in part)
+        assert flat == list(range(len(lengths)))  # every sample exactly once
+        cfg = CONFIGS[name].config
+        loads = [sum(sample_cost(lengths[i], cfg.d_model, cfg.ffn_dim) for i in part) for part in gathered]
+        assert max(loads) / (sum(loads) / 2) < 1.05  # balanced within 5%
+    assert out["C5"] == [(0, 131072), (131072, 262144)]
+
+
+def test_token_range_rejects_uneven_split():
+    with pytest.raises(ValueError):
+        token_range(1000, 3, 0)
