@@ -96,6 +96,10 @@ class B200Transformer(nn.Module):
         self._handle: Optional[_Handle] = None
         self._packed_sig: Optional[Tuple] = None
         self._workspaces: Dict[Tuple, torch.Tensor] = {}
+        # CUDA-graph replay of the whole forward (opt-in, see enable_cuda_graphs)
+        self.cuda_graphs = False
+        self._graphs: Dict[Tuple, Tuple] = {}
+        self.graph_kernel_launches = 0  # kernels replayed through graphs (libtj counts host launches only)
 
     # ---------------------------------------------------------------- packing
     def _param_signature(self, device: torch.device) -> Tuple:
@@ -163,7 +167,23 @@ class B200Transformer(nn.Module):
         if hasattr(self, "_workspaces"):
             self._packed_sig = None
             self._workspaces = {}
+            self._graphs = {}
         return result
+
+    def enable_cuda_graphs(self, enabled: bool = True) -> "B200Transformer":
+        """Replay the whole forward as one CUDA graph per (input, mask, shape).
+
+        The first call with given input/mask tensors runs normally, then
+        captures the launch sequence; later calls with the SAME tensors
+        (their current contents) replay it.  The output is a buffer owned by
+        the graph and overwritten by the next replay -- the same contract as
+        the reference dispatcher's CUDA-graph mode (torch.compile
+        "reduce-overhead", src/dispatcher.py:48-62).
+        """
+        self.cuda_graphs = enabled
+        if not enabled:
+            self._graphs = {}
+        return self
 
     # ---------------------------------------------------------------- forward
     def forward(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
@@ -176,6 +196,7 @@ class B200Transformer(nn.Module):
         in_dtype = x.dtype
         xf = x if (x.dtype == torch.float32 and x.is_contiguous()) else x.float().contiguous()
         mask_ptr = None
+        m = None
         if valid_token_mask is not None:
             if valid_token_mask.shape != (batch, seq_len):
                 raise ValueError("valid_token_mask must be [B, N]")
@@ -188,12 +209,35 @@ class B200Transformer(nn.Module):
             mask_ptr = m.data_ptr()
         handle = self._ensure_packed(device)
         ws = self._workspace(handle, batch, seq_len, device)
+        route = _ROUTES[self.attention_route]
+
+        def launch(out: torch.Tensor) -> None:
+            stream = torch.cuda.current_stream(device)
+            with torch.cuda.device(device):
+                _lib.call("tj_forward", handle.ptr, xf.data_ptr(), mask_ptr, out.data_ptr(), batch, seq_len,
+                          route, ws.data_ptr(), ws.numel(), ctypes.c_void_p(stream.cuda_stream))
+
+        if self.cuda_graphs and xf is x and (valid_token_mask is None or m is valid_token_mask):
+            key = (device, xf.data_ptr(), mask_ptr, batch, seq_len, route, ws.data_ptr())
+            entry = self._graphs.get(key)
+            if entry is None:
+                out = torch.empty((batch, seq_len, self.config.d_model), dtype=torch.float32, device=device)
+                launch(out)  # first call: also performs the library's one-time set-up outside capture
+                torch.cuda.synchronize(device)
+                before = ctypes.c_longlong()
+                _lib.call("tj_launch_count", handle.ptr, ctypes.byref(before))
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph):
+                    launch(out)
+                after = ctypes.c_longlong()
+                _lib.call("tj_launch_count", handle.ptr, ctypes.byref(after))
+                entry = (graph, out, ws, int(after.value - before.value))
+                self._graphs[key] = entry
+            entry[0].replay()
+            self.graph_kernel_launches += entry[3]
+            return entry[1]
         out = torch.empty((batch, seq_len, self.config.d_model), dtype=torch.float32, device=device)
-        stream = torch.cuda.current_stream(device)
-        with torch.cuda.device(device):
-            _lib.call("tj_forward", handle.ptr, xf.data_ptr(), mask_ptr, out.data_ptr(), batch, seq_len,
-                      _ROUTES[self.attention_route], ws.data_ptr(), ws.numel(),
-                      ctypes.c_void_p(stream.cuda_stream))
+        launch(out)
         return out if in_dtype == torch.float32 else out.to(in_dtype)
 
     def device_error(self) -> int:

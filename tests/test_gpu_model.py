@@ -192,3 +192,24 @@ def test_fp16_model_interface():
         ref = oracle(x.half().float(), mask)
         v = check_outputs(ref, got.float(), rtol=0.02, atol=0.01)
         assert v.passed
+
+
+def test_cuda_graph_replay():
+    """Graph replay gives the eager result and follows in-place input updates."""
+    cfg = EncoderShape(4, 512, 256, 8, 1024, 2, True)
+    oracle, cand = _models(cfg, 1.0)
+    eager = CANDIDATE.model_factory(cfg)
+    eager.load_state_dict(oracle.state_dict(), strict=True)
+    eager = eager.to(DEV).eval()
+    cand.enable_cuda_graphs()
+    with torch.inference_mode():
+        x, mask = generate_random_case(cfg, DEV, torch.float32, 1234, 0.5)
+        first = cand(x, mask).clone()   # eager run + capture
+        second = cand(x, mask).clone()  # replay
+        assert torch.equal(first, second)
+        assert torch.equal(second, eager(x, mask))
+        x2, _ = generate_random_case(cfg, DEV, torch.float32, 1235, 0.5)
+        x.copy_(x2.masked_fill(~mask[..., None], 0))
+        third = cand(x, mask)
+        assert torch.equal(third, eager(x, mask))
+        assert cand.graph_kernel_launches > 0
