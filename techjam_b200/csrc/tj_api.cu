@@ -3,6 +3,7 @@
 #include <cudaTypedefs.h>
 
 #include <cstdarg>
+#include <cstdlib>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -107,6 +108,12 @@ int make_map_f16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t col
 
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
+// 2-SM GEMM switch (TJ_PAIR_GEMM=0 turns it off, for A/B comparisons).
+const bool g_use_pair_gemm = [] {
+  const char* e = std::getenv("TJ_PAIR_GEMM");
+  return !(e && e[0] == '0');
+}();
+
 // ------------------------------------------------------------------ kernel launchers
 template <int BN, int EPI>
 int launch_gemm_bn(const CUtensorMap& ta, const CUtensorMap& tw, const tj::GemmParams& p, int sms, cudaStream_t st) {
@@ -129,10 +136,57 @@ int launch_gemm_bn(const CUtensorMap& ta, const CUtensorMap& tw, const tj::GemmP
   return TJ_OK;
 }
 
+// 2-SM GEMM (cluster of 2, tcgen05 cta_group::2): grid = 2 x co-resident pairs.
+template <int EPI>
+int launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tw, const tj::GemmParams& p, int pair_tiles,
+                     cudaStream_t st) {
+  using Cfg = tj::Gemm2Cfg;
+  auto kern = tj::gemm_tc2_kernel<EPI>;
+  static int max_pairs[64] = {};
+  int dev = 0;
+  TJ_CUDA(cudaGetDevice(&dev));
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(Cfg::kThreads);
+  cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (max_pairs[dev] == 0) {
+    TJ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes));
+    cfg.gridDim = dim3(2);
+    int n = 0;
+    TJ_CUDA(cudaOccupancyMaxActiveClusters(&n, kern, &cfg));
+    max_pairs[dev] = n > 0 ? n : 1;
+  }
+  const int pairs = std::min(pair_tiles, max_pairs[dev]);
+  if (pairs <= 0) return TJ_OK;
+  cfg.gridDim = dim3(2 * pairs);
+  TJ_CUDA(cudaLaunchKernelEx(&cfg, kern, ta, tw, p));
+  return TJ_OK;
+}
+
 template <int EPI>
 int launch_gemm(const void* a, const void* w, const tj::GemmParams& p, int sms, cudaStream_t st) {
   CUtensorMap ta, tw;
   TJ_CHECK(make_map_f16(&ta, a, p.M, p.K, tj::kGemmBM, tj::kGemmBK, 128));
+  // 2-SM tiles (256 x 256 per CTA pair) when N allows and there is at least a
+  // wave of them; otherwise 1-CTA tiles.
+  {
+    const long long m_tiles = (p.M + 127) / 128;
+    const long long pair_tiles = ((m_tiles + 1) / 2) * (p.N / 256);
+    // Pairs run their epilogues in lock-step; with a short mainloop (K < 1024)
+    // the GELU epilogue dominates and the 1-CTA kernel is faster.
+    const bool epilogue_bound = EPI == tj::kEpiGelu && p.K < 1024;
+    if (g_use_pair_gemm && p.N % 256 == 0 && pair_tiles >= sms / 2 && !epilogue_bound) {
+      TJ_CHECK(make_map_f16(&tw, w, p.N, p.K, 128, tj::kGemmBK, 128));
+      return launch_gemm_pair<EPI>(ta, tw, p, (int)pair_tiles, st);
+    }
+  }
   // Wide tiles when there are enough of them to fill the machine, else 128.
   const long long m_tiles = (p.M + 127) / 128;
   const bool wide = (p.N % 256 == 0) && (m_tiles * (p.N / 256) >= sms);

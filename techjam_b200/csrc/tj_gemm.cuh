@@ -270,4 +270,166 @@ __global__ void __launch_bounds__(320, 1)
   if (warp == 1) tmem_dealloc(tmem_base, Cfg::kTmemCols);
 }
 
+// ------------------------------------------------------------------ 2-SM variant
+// A cluster of 2 CTAs computes 256 x 256 output tiles with tcgen05.mma
+// cta_group::2: each CTA stages its own 128 rows of A and 128 of the 256 W
+// rows (32 KB per 64-deep k-block instead of 48 KB for a 128 x 256 tile),
+// which buys a 6-deep ring in the same shared memory.  The pair may take any
+// two live 128-row tiles (they need not be adjacent); an odd live count
+// leaves the last pair's second half reading the zero-filled rows past M.
+//   warp 0: TMA (both CTAs; completion on the even CTA's `full` barrier)
+//   warp 1: even CTA's single thread issues the 2-SM MMAs; commits are
+//           multicast to both CTAs (smem slot free / accumulator ready)
+//   warps 2..9: epilogue of this CTA's 128 rows; done -> even CTA's acc_empty
+struct Gemm2Cfg {
+  static constexpr int kBN = 256;                       // N per pair tile (128 W rows per CTA)
+  static constexpr int kStageBytes = 2 * kGemmBM * kGemmBK * 2;  // A 16 KB + W half 16 KB
+  static constexpr int kStages = 6;
+  static constexpr int kTmemCols = 512;                 // 2 x 256-column accumulators
+  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 256;
+  static constexpr int kThreads = 320;
+  static constexpr int kEpiThreads = 256;
+};
+
+template <int EPI>
+__global__ void __launch_bounds__(320, 1)
+    gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
+                    const GemmParams p) {
+  using Cfg = Gemm2Cfg;
+  constexpr int S = Cfg::kStages;
+  constexpr int BN = Cfg::kBN;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes);
+  uint64_t* full = bars;              // [S]  (even CTA's copy is the live one)
+  uint64_t* empty = bars + S;         // [S]
+  uint64_t* acc_full = bars + 2 * S;  // [2]
+  uint64_t* acc_empty = acc_full + 2; // [2] (even CTA's copy is the live one)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();  // 0 = even CTA (issues the MMAs)
+  const int pair = blockIdx.x >> 1;
+  const int n_pairs = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) { mbar_init(full + i, 1); mbar_init(empty + i, 1); }
+    for (int i = 0; i < 2; ++i) { mbar_init(acc_full + i, 1); mbar_init(acc_empty + i, 2 * Cfg::kEpiThreads); }
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, Cfg::kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // both CTAs' barriers exist before any remote arrive or multicast commit
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int n_live = __ldg(p.n_live);
+  const int n_tiles = p.N / BN;
+  const int total = ((n_live + 1) >> 1) * n_tiles;  // pair tiles
+  const int k_blocks = (p.K + kGemmBK - 1) / kGemmBK;
+  // this CTA's 128-row tile of pair tile t (ghost tiles read rows past M: zero fill)
+  auto my_mtile = [&](int t, bool& ghost) {
+    const int li = 2 * (t / n_tiles) + (int)rank;
+    ghost = li >= n_live;
+    return ghost ? (p.M + kGemmBM - 1) / kGemmBM : __ldg(p.tile_list + li);
+  };
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------------------------------------ TMA producer (both CTAs)
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmW);
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int t = pair; t < total && ok; t += n_pairs) {
+      bool ghost;
+      const int mt = my_mtile(t, ghost);
+      const int nt = t % n_tiles;
+      for (int kb = 0; kb < k_blocks; ++kb) {
+        if (!mbar_wait(empty + stage, phase ^ 1u, p.err, kErrGemmProducer)) { ok = false; break; }
+        uint8_t* sa = smem + stage * Cfg::kStageBytes;
+        uint8_t* sb = sa + kGemmBM * kGemmBK * 2;
+        const uint32_t lb = pair_leader_bar(full + stage);
+        if (rank == 0) mbar_expect_tx(full + stage, 2 * Cfg::kStageBytes);  // both CTAs' bytes
+        tma_load_2d_pair(sa, &tmA, lb, kb * kGemmBK, mt * kGemmBM);
+        tma_load_2d_pair(sb, &tmW, lb, kb * kGemmBK, nt * BN + (int)rank * 128);
+        if (++stage == S) { stage = 0; phase ^= 1u; }
+      }
+    }
+  } else if (warp == 1 && lane == 0 && rank == 0) {
+    // ------------------------------------------------------------ 2-SM MMA issuer (even CTA)
+    constexpr uint32_t idesc = idesc_f16_f32(256, BN, false, false);
+    int stage = 0;
+    uint32_t phase = 0;
+    int abuf = 0;
+    uint32_t aphase = 0;
+    bool ok = true;
+    for (int t = pair; t < total && ok; t += n_pairs) {
+      if (!mbar_wait(acc_empty + abuf, aphase ^ 1u, p.err, kErrGemmMma)) break;
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + abuf * BN;
+      for (int kb = 0; kb < k_blocks; ++kb) {
+        if (!mbar_wait(full + stage, phase, p.err, kErrGemmMma)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t sa = smem_u32(smem + stage * Cfg::kStageBytes);
+        const uint32_t sb = sa + kGemmBM * kGemmBK * 2;
+#pragma unroll
+        for (int ks = 0; ks < kGemmBK / 16; ++ks) {
+          const uint64_t ad = smem_desc(sa + ks * 32, 16, 1024, 128);
+          const uint64_t bd = smem_desc(sb + ks * 32, 16, 1024, 128);
+          umma_f16_ss_pair(d_tmem, ad, bd, idesc, (kb | ks) != 0);
+        }
+        umma_commit_pair_both(empty + stage);
+        if (++stage == S) { stage = 0; phase ^= 1u; }
+      }
+      if (!ok) break;
+      umma_commit_pair_both(acc_full + abuf);
+      if (++abuf == 2) { abuf = 0; aphase ^= 1u; }
+    }
+  } else if (warp >= 2) {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
+    constexpr int kChunks = BN / 64;
+    const int row_in_tile = quarter * 32 + lane;
+    const uint32_t leader_acc_empty0 = map_to_rank(acc_empty, 0);
+    int abuf = 0;
+    uint32_t aphase = 0;
+    for (int t = pair; t < total; t += n_pairs) {
+      bool ghost;
+      const int mt = my_mtile(t, ghost);
+      const int nt = t % n_tiles;
+      const int row = mt * kGemmBM + row_in_tile;
+      const bool in_range = !ghost && row < p.M;
+      const bool valid = in_range && row_is_valid(p, row);
+      const int colh = nt * BN + half * (BN / 2);
+      ChunkOperands ops[2];
+      if (in_range) load_chunk_operands<EPI>(p, row, valid, colh, ops[0]);
+      if (!mbar_wait(acc_full + abuf, aphase, p.err, kErrGemmEpilogue)) break;
+      tc_fence_after();
+      const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + abuf * BN + half * (BN / 2);
+#pragma unroll
+      for (int c = 0; c < kChunks; ++c) {
+        const int col0 = colh + c * 32;
+        if (c + 1 < kChunks && in_range) load_chunk_operands<EPI>(p, row, valid, col0 + 32, ops[(c + 1) & 1]);
+        uint32_t acc[32];
+        tmem_ld32(taddr + c * 32, acc);
+        tmem_ld_wait();
+        if (in_range) epilogue_chunk<EPI>(p, row, valid, col0, acc, ops[c & 1]);
+      }
+      tc_fence_before();
+      mbar_arrive_cluster(leader_acc_empty0 + (uint32_t)(abuf * sizeof(uint64_t)));
+      if (++abuf == 2) { abuf = 0; aphase ^= 1u; }
+    }
+  }
+  tc_fence_before();
+  cluster_sync();  // no CTA leaves while its pair partner may still touch its barriers or smem
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc_pair(tmem_base, Cfg::kTmemCols);
+}
+
 }  // namespace tj

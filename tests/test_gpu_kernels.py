@@ -77,8 +77,10 @@ def _gemm_case(b, n, k, nout, seed, lo=1):
 
 
 @pytest.mark.parametrize("b,n,k,nout", [(3, 200, 256, 512), (2, 512, 1024, 1024), (16, 1024, 1024, 4096),
-                                         (4, 256, 2048, 512)])
+                                         (4, 256, 2048, 512), (3, 1000, 512, 4096), (5, 700, 1024, 3072)])
 def test_gemm_gelu_and_plain(b, n, k, nout):
+    """Small shapes take the 1-CTA kernel; the large ones the 2-SM pair kernel
+    (ragged lengths give odd live-tile counts: the pair's ghost half)."""
     a, w, bias, mask, ref = _gemm_case(b, n, k, nout, seed=b * 7 + n)
     info = ops.prepare_mask(mask.to(DEV), b, n)
     valid = mask.reshape(-1)
