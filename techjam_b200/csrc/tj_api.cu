@@ -114,6 +114,14 @@ const bool g_use_pair_gemm = [] {
   return !(e && e[0] == '0');
 }();
 
+// Persistent attention for head_dim <= 64: by default for sequences of at
+// most two query-tile pairs; TJ_ATTN_PERSIST=0 / 1 forces it off / on (A/B).
+const int g_attn_persist = [] {
+  const char* e = std::getenv("TJ_ATTN_PERSIST");
+  return (e && (e[0] == '0' || e[0] == '1')) ? e[0] - '0' : -1;
+}();
+constexpr int kPersistMaxPairs = 2;
+
 // ------------------------------------------------------------------ kernel launchers
 template <int BN, int EPI>
 int launch_gemm_bn(const CUtensorMap& ta, const CUtensorMap& tw, const tj::GemmParams& p, int sms, cudaStream_t st) {
@@ -218,17 +226,39 @@ int launch_attn_hd(const void* q, const void* k, const void* v, const tj::AttnPa
   TJ_CHECK(make_map_f16(&tq, q, rows, HD, 128, Cfg::kAtomCols, Cfg::kSw));
   TJ_CHECK(make_map_f16(&tk, k, kv_rows, HD, 128, Cfg::kAtomCols, Cfg::kSw));
   TJ_CHECK(make_map_f16(&tv, v, kv_rows, HD, 128, Cfg::kAtomCols, Cfg::kSw));
-  auto kern = tj::attn_fwd_kernel<HD>;
-  static bool attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (!attr_set[dev]) {
-    TJ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes));
-    attr_set[dev] = true;
-  }
   const int q_tiles = (p.S + 127) / 128;
-  dim3 grid((q_tiles + 1) / 2, B * p.H);  // one CTA per pair of 128-query tiles
-  kern<<<grid, Cfg::kThreads, Cfg::kSmemBytes, st>>>(tq, tk, tv, p);
+  const int n_pairs = (q_tiles + 1) / 2;
+  bool persistent = false;
+  if constexpr (Cfg::kPSeparate)
+    persistent = g_attn_persist < 0 ? n_pairs <= kPersistMaxPairs : g_attn_persist == 1;
+  if (persistent) {
+    if constexpr (Cfg::kPSeparate) {
+      // one CTA per SM over a heavy-first list of (pair, head, sample) items
+      static bool attr_set[64] = {};
+      auto kern = tj::attn_fwd_persistent_kernel<HD>;
+      if (!attr_set[dev]) {
+        TJ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemPersist));
+        attr_set[dev] = true;
+      }
+      DeviceInfo di;
+      TJ_CHECK(device_info(&di));
+      const long long items = (long long)n_pairs * B * p.H;
+      if (items > 0x7fffffffLL - 2LL * di.sms) return fail(TJ_ERR_UNSUPPORTED, "too many attention work items");
+      const int grid = (int)std::min<long long>(items, di.sms);
+      kern<<<grid, Cfg::kThreads, Cfg::kSmemPersist, st>>>(tq, tk, tv, p, n_pairs, (int)items);
+    }
+  } else {
+    static bool attr_set[64] = {};
+    auto kern = tj::attn_fwd_kernel<HD>;
+    if (!attr_set[dev]) {
+      TJ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes));
+      attr_set[dev] = true;
+    }
+    dim3 grid(n_pairs, B * p.H);  // one CTA per pair of 128-query tiles
+    kern<<<grid, Cfg::kThreads, Cfg::kSmemBytes, st>>>(tq, tk, tv, p);
+  }
   TJ_CUDA(cudaGetLastError());
   return TJ_OK;
 }

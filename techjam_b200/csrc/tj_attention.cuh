@@ -62,6 +62,7 @@ struct AttnCfg {
   static constexpr int kTile = 128 * HD * 2;
   static constexpr int kStages = HD >= 128 ? 2 : (HD == 64 ? 4 : 6);
   static constexpr int kSmemBytes = 2 * kTile + kStages * 2 * kTile + 1024 + 256;
+  static constexpr int kSmemPersist = 4 * kTile + kStages * 2 * kTile + 1024 + 512;  // Q double-buffered
   static constexpr int kTmemCols = 512;
   // TMEM columns.  HD <= 64: S0 S1 (fp32) | P0 P1 (fp16 pairs) | O0 O1, so the
   // next S can be computed while P is still being consumed.  HD = 128: P
@@ -292,14 +293,7 @@ __global__ void __launch_bounds__(320, 1)
           if (dead) s[i] = __float_as_uint(-INFINITY);
         }
       }
-      // row max with 8 independent chains
-      float mx8[8];
-#pragma unroll
-      for (int k = 0; k < 8; ++k) mx8[k] = __uint_as_float(s[k]);
-#pragma unroll
-      for (int i = 8; i < 128; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], __uint_as_float(s[i]));
-      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+      const float mx = row_max128(s);
       const float m_tile = mx * sl2;
       const bool grow = m_tile > m_run + Cfg::kRescaleLog2;
       float alpha = 1.0f;
@@ -308,16 +302,8 @@ __global__ void __launch_bounds__(320, 1)
         m_run = m_tile;
       }
       const float msub = m_run == -INFINITY ? 0.0f : m_run;
-      float sum8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      // P packs two fp16 per 32-bit column; the packed words overwrite s[]
-      // in place (word i only consumes s[2i], s[2i+1], both >= i).
-#pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        const float p0 = fast_exp2(fmaf(__uint_as_float(s[2 * i]), sl2, -msub));
-        const float p1 = fast_exp2(fmaf(__uint_as_float(s[2 * i + 1]), sl2, -msub));
-        sum8[i & 7] += p0 + p1;
-        s[i] = pack_half2(p0, p1);
-      }
+      // P packs two fp16 per 32-bit column, written over s[0..63]
+      const float rowsum = exp_pack_rowsum(s, sl2, msub);
       if constexpr (Cfg::kPSeparate) {
         // P_t and O_t are free once PV_t(j-1) has retired
         if (j > 0 && !mbar_wait(pv_done + t, (j - 1) & 1, p.err, kErrAttnSoftmax)) { ok = false; break; }
@@ -325,7 +311,6 @@ __global__ void __launch_bounds__(320, 1)
       }
       tmem_st32(p_col, *reinterpret_cast<uint32_t(*)[32]>(s));
       tmem_st32(p_col + 32, *reinterpret_cast<uint32_t(*)[32]>(s + 32));
-      const float rowsum = ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
       l_run = l_run * alpha + rowsum;
       // Rescale this row of O in TMEM (the whole warp takes part if any lane
       // needs it).  PV_t(j-1) has retired, so O is stable.
@@ -366,6 +351,333 @@ __global__ void __launch_bounds__(320, 1)
           }
         }
       }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 9) tmem_dealloc(tmem, Cfg::kTmemCols);
+}
+
+}  // namespace tj
+
+namespace tj {
+
+// ------------------------------------------------------------------ persistent variant
+// Same arithmetic as attn_fwd_kernel (head_dim <= 64, P in its own TMEM
+// columns), but one CTA per SM walks a heavy-first list of work items
+// (query-tile pair, head, sample) round-robin: item i covers pair
+// (np-1 - i/BH) of head-sample i%BH for causal attention, so the longest
+// items start first.  Every role decodes the same item sequence itself.
+// It pays off where items are short (a pair or two of query tiles per
+// sequence), which the one-CTA-per-pair grid spends on CTA start-up.
+// TMEM and barriers are set up once; Q is double-buffered so the next item's
+// Q and K/V stream in while the current one finishes, and every barrier phase
+// is tracked with running use counters across items.
+template <int HD>
+__global__ void __launch_bounds__(320, 1)
+    attn_fwd_persistent_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                               const __grid_constant__ CUtensorMap tmV, const AttnParams p, int n_pairs,
+                               int n_items) {
+  using Cfg = AttnCfg<HD>;
+  static_assert(Cfg::kPSeparate, "persistent variant needs P in its own TMEM columns");
+  constexpr int ST = Cfg::kStages;
+  static_assert(8 * (16 + 2 * ST) + 4 <= 512, "barrier region exceeds its share of kSmemPersist");
+  if (error_raised(p.err)) return;
+  const int BH = p.B * p.H;
+  const bool gated = p.poly_admit != nullptr && *reinterpret_cast<const volatile int*>(p.poly_admit) != 0;
+  // an admitted polynomial route leaves only the exact prefix's pairs here
+  const int np = gated ? min(n_pairs, p.exact_pairs) : n_pairs;
+  n_items = np * BH;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;                         // [2 buffers][2 tiles][tile]
+  uint8_t* sKV = sQ + 4 * Cfg::kTile;         // stage s: K at s*2*kTile, V after it
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sKV + ST * 2 * Cfg::kTile);
+  uint64_t* q_full = bars;                    // [2]
+  uint64_t* q_empty = q_full + 2;             // [2]
+  uint64_t* kv_full = q_empty + 2;            // [ST]
+  uint64_t* kv_empty = kv_full + ST;          // [ST]
+  uint64_t* s_full = kv_empty + ST;           // [2 tiles]
+  uint64_t* s_free = s_full + 2;
+  uint64_t* p_full = s_free + 2;
+  uint64_t* pv_done = p_full + 2;
+  uint64_t* o_final = pv_done + 2;
+  uint64_t* o_free = o_final + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_free + 2);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) { mbar_init(q_full + i, 1); mbar_init(q_empty + i, 1); }
+    for (int i = 0; i < ST; ++i) { mbar_init(kv_full + i, 1); mbar_init(kv_empty + i, 1); }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(s_full + i, 1);
+      mbar_init(s_free + i, 128);
+      mbar_init(p_full + i, 128);
+      mbar_init(pv_done + i, 1);
+      mbar_init(o_final + i, 1);
+      mbar_init(o_free + i, 128);
+    }
+    fence_mbar_init();
+  }
+  if (warp == 9) {
+    tmem_alloc(tmem_slot, Cfg::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  // Work item decode, identical in every role.
+  struct Item {
+    int b, h, bh, q0, qg0, len, nkv0, nkv1, n_kv;
+    bool has1, general;
+  };
+  auto decode = [&](int i, Item& it) -> bool {
+    const int pair = p.causal ? np - 1 - i / BH : i / BH;
+    it.bh = i % BH;
+    it.b = it.bh / p.H;
+    it.h = it.bh - it.b * p.H;
+    it.len = __ldg(p.lengths + it.b);
+    it.q0 = 2 * pair;
+    it.qg0 = p.q_pos0 / 128 + it.q0;
+    if (it.qg0 * 128 >= it.len || it.q0 * 128 >= p.S) return false;
+    it.has1 = (it.qg0 + 1) * 128 < it.len && (it.q0 + 1) * 128 < p.S;
+    const int kv_all = (it.len + 127) / 128;
+    it.nkv0 = p.causal ? it.qg0 + 1 : kv_all;
+    it.nkv1 = it.has1 ? (p.causal ? it.qg0 + 2 : kv_all) : 0;
+    it.n_kv = it.nkv0 > it.nkv1 ? it.nkv0 : it.nkv1;
+    it.general = p.mask != nullptr && __ldg(p.general + it.b) != 0;
+    return true;
+  };
+  auto kv_row = [&](const Item& it, int j) {
+    const int pos = j * 128;
+    const int shard = pos / p.kv_shard;
+    return ((shard * p.B + it.b) * p.H + it.h) * p.kv_shard + (pos - shard * p.kv_shard);
+  };
+
+  if (warp == 8) {
+    if (lane == 0) {
+      // ---------------------------------------------------------- producer
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      int kvc = 0, nitem = 0;
+      bool ok = true;
+      for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x) {
+        Item it;
+        if (!decode(i, it)) continue;
+        const int qb = nitem & 1;
+        if (nitem >= 2 && !mbar_wait(q_empty + qb, ((nitem >> 1) - 1) & 1, p.err, kErrAttnProducer)) break;
+        mbar_expect_tx(q_full + qb, (it.has1 ? 2 : 1) * Cfg::kTile);
+        for (int t = 0; t < (it.has1 ? 2 : 1); ++t)
+#pragma unroll
+          for (int a = 0; a < Cfg::kAtoms; ++a)
+            tma_load_2d(sQ + (qb * 2 + t) * Cfg::kTile + a * Cfg::kAtomBytes, &tmQ, q_full + qb,
+                        a * Cfg::kAtomCols, it.bh * p.S + (it.q0 + t) * 128);
+        for (int j = 0; j < it.n_kv; ++j) {
+          const int g = kvc + j, st = g % ST;
+          if (!mbar_wait(kv_empty + st, ((g / ST) & 1) ^ 1, p.err, kErrAttnProducer)) { ok = false; break; }
+          uint8_t* sk = sKV + st * 2 * Cfg::kTile;
+          mbar_expect_tx(kv_full + st, 2 * Cfg::kTile);
+#pragma unroll
+          for (int a = 0; a < Cfg::kAtoms; ++a) {
+            tma_load_2d(sk + a * Cfg::kAtomBytes, &tmK, kv_full + st, a * Cfg::kAtomCols, kv_row(it, j));
+            tma_load_2d(sk + Cfg::kTile + a * Cfg::kAtomBytes, &tmV, kv_full + st, a * Cfg::kAtomCols,
+                        kv_row(it, j));
+          }
+        }
+        kvc += it.n_kv;
+        ++nitem;
+      }
+    }
+  } else if (warp == 9) {
+    if (lane == 0) {
+      // ---------------------------------------------------------- MMA issuer
+      constexpr uint32_t idesc_qk = idesc_f16_f32(128, 128, false, false);
+      constexpr uint32_t idesc_pv = idesc_f16_f32(128, HD, false, true);
+      int kvc = 0, nitem = 0;
+      int cs[2] = {0, 0};  // S_t computed so far
+      int ci[2] = {0, 0};  // items in which tile t took part so far
+      bool ok = true;
+      for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x) {
+        Item it;
+        if (!decode(i, it)) continue;
+        const int qb = nitem & 1;
+        const int nkv[2] = {it.nkv0, it.nkv1};
+        if (!mbar_wait(q_full + qb, (nitem >> 1) & 1, p.err, kErrAttnMma)) break;
+        const uint32_t q_addr = smem_u32(sQ + qb * 2 * Cfg::kTile);
+        auto kv_addr = [&](int j) { return smem_u32(sKV + ((kvc + j) % ST) * 2 * Cfg::kTile); };
+        auto issue_s = [&](int t, uint32_t k_addr) {
+          const uint32_t qa = q_addr + t * Cfg::kTile;
+#pragma unroll
+          for (int ks = 0; ks < HD / 16; ++ks) {
+            const int atom = (ks * 16) / Cfg::kAtomCols;
+            const int within = ((ks * 16) % Cfg::kAtomCols) * 2;
+            const uint64_t ad = smem_desc(qa + atom * Cfg::kAtomBytes + within, 16, 8 * Cfg::kRowB, Cfg::kSw);
+            const uint64_t bd = smem_desc(k_addr + atom * Cfg::kAtomBytes + within, 16, 8 * Cfg::kRowB, Cfg::kSw);
+            umma_f16_ss(tmem + Cfg::kColS + t * 128, ad, bd, idesc_qk, ks != 0);
+          }
+          umma_commit(s_full + t);
+        };
+        // first key tile: S_t(0) once the previous item's last S_t has been read
+        {
+          const int g = kvc;
+          if (!mbar_wait(kv_full + g % ST, (g / ST) & 1, p.err, kErrAttnMma)) break;
+          tc_fence_after();
+          for (int t = 0; t < 2 && ok; ++t) {
+            if (nkv[t] == 0) continue;
+            if (cs[t] > 0 && !mbar_wait(s_free + t, (cs[t] - 1) & 1, p.err, kErrAttnMma)) { ok = false; break; }
+            tc_fence_after();
+            issue_s(t, kv_addr(0));
+          }
+        }
+        for (int j = 0; j < it.n_kv && ok; ++j) {
+          if (j + 1 < it.n_kv) {
+            const int g = kvc + j + 1;
+            if (!mbar_wait(kv_full + g % ST, (g / ST) & 1, p.err, kErrAttnMma)) { ok = false; break; }
+            for (int t = 0; t < 2 && ok; ++t) {
+              if (j + 1 >= nkv[t]) continue;
+              if (!mbar_wait(s_free + t, (cs[t] + j) & 1, p.err, kErrAttnMma)) { ok = false; break; }
+              tc_fence_after();
+              issue_s(t, kv_addr(j + 1));
+            }
+          }
+          for (int t = 0; t < 2 && ok; ++t) {
+            if (j >= nkv[t]) continue;
+            if (!mbar_wait(p_full + t, (cs[t] + j) & 1, p.err, kErrAttnMma)) { ok = false; break; }
+            if (j == 0 && ci[t] > 0 && !mbar_wait(o_free + t, (ci[t] - 1) & 1, p.err, kErrAttnMma)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t o_tmem = tmem + Cfg::kColO + t * HD;
+            const uint32_t p_tmem = tmem + Cfg::kColP + t * 64;
+            const uint32_t v_addr = kv_addr(j) + Cfg::kTile;
+#pragma unroll
+            for (int ks = 0; ks < 8; ++ks) {
+              const uint64_t bd = smem_desc(v_addr + ks * 16 * Cfg::kRowB, Cfg::kAtomBytes, 8 * Cfg::kRowB, Cfg::kSw);
+              umma_f16_ts(o_tmem, p_tmem + ks * 8, bd, idesc_pv, (j | ks) != 0);
+            }
+            umma_commit(pv_done + t);
+            if (j == nkv[t] - 1) umma_commit(o_final + t);
+          }
+          umma_commit(kv_empty + (kvc + j) % ST);
+        }
+        umma_commit(q_empty + qb);
+        kvc += it.n_kv;
+        for (int t = 0; t < 2; ++t) {
+          cs[t] += nkv[t];
+          ci[t] += nkv[t] > 0 ? 1 : 0;
+        }
+        ++nitem;
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ softmax + epilogue
+    const int t = warp >> 2;
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const uint32_t s_col = tmem + lane_off + Cfg::kColS + t * 128;
+    const uint32_t p_col = tmem + lane_off + Cfg::kColP + t * 64;
+    const uint32_t o_col = tmem + lane_off + Cfg::kColO + t * HD;
+    const float sl2 = p.scale_log2;
+    int cs = 0, ci = 0;
+    bool ok = true;
+    for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x) {
+      Item it;
+      if (!decode(i, it)) continue;
+      const int nkv_t = t == 0 ? it.nkv0 : it.nkv1;
+      if (nkv_t == 0) continue;
+      const int qt = it.q0 + t;
+      const int qrow = qt * 128 + r;
+      const uint8_t* kmask = it.general ? p.mask + (size_t)it.b * p.S : nullptr;
+      float m_run = -INFINITY, l_run = 0.0f;
+      for (int j = 0; j < nkv_t; ++j) {
+        const int u = cs + j;  // global use index of S_t / P_t
+        if (!mbar_wait(s_full + t, u & 1, p.err, kErrAttnSoftmax)) { ok = false; break; }
+        tc_fence_after();
+        uint32_t s[128];
+        tmem_ld32(s_col + 0, *reinterpret_cast<uint32_t(*)[32]>(s + 0));
+        tmem_ld32(s_col + 32, *reinterpret_cast<uint32_t(*)[32]>(s + 32));
+        tmem_ld32(s_col + 64, *reinterpret_cast<uint32_t(*)[32]>(s + 64));
+        tmem_ld32(s_col + 96, *reinterpret_cast<uint32_t(*)[32]>(s + 96));
+        tmem_ld_wait();
+        tc_fence_before();
+        mbar_arrive(s_free + t);
+        const int kbase = j * 128;
+        const bool diag = p.causal && j == it.qg0 + t;
+        const bool tail = kbase + 128 > it.len;
+        if (diag || tail || kmask) {
+          const int lim_causal = diag ? r : 127;
+          const int lim_len = it.len - kbase - 1;
+          const int lim = lim_causal < lim_len ? lim_causal : lim_len;
+#pragma unroll
+          for (int i2 = 0; i2 < 128; ++i2) {
+            bool dead = i2 > lim;
+            if (kmask) dead = dead || (kmask[kbase + i2] == 0);
+            if (dead) s[i2] = __float_as_uint(-INFINITY);
+          }
+        }
+        const float mx = row_max128(s);
+        const float m_tile = mx * sl2;
+        const bool grow = m_tile > m_run + Cfg::kRescaleLog2;
+        float alpha = 1.0f;
+        if (grow) {
+          alpha = fast_exp2(m_run - m_tile);
+          m_run = m_tile;
+        }
+        const float msub = m_run == -INFINITY ? 0.0f : m_run;
+        const float rowsum = exp_pack_rowsum(s, sl2, msub);
+        // P_t and O_t are free once the previous PV_t (this item's or the last item's) retired
+        if (u > 0 && !mbar_wait(pv_done + t, (u - 1) & 1, p.err, kErrAttnSoftmax)) { ok = false; break; }
+        tc_fence_after();
+        tmem_st32(p_col, *reinterpret_cast<uint32_t(*)[32]>(s));
+        tmem_st32(p_col + 32, *reinterpret_cast<uint32_t(*)[32]>(s + 32));
+        l_run = l_run * alpha + rowsum;
+        if (j > 0 && __any_sync(0xffffffffu, grow)) {
+#pragma unroll
+          for (int c = 0; c < HD / 32; ++c) {
+            uint32_t o[32];
+            tmem_ld32(o_col + c * 32, o);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i2 = 0; i2 < 32; ++i2) o[i2] = __float_as_uint(__uint_as_float(o[i2]) * alpha);
+            tmem_st32(o_col + c * 32, o);
+          }
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(p_full + t);
+      }
+      if (!ok) break;
+      if (!mbar_wait(o_final + t, ci & 1, p.err, kErrAttnSoftmax)) { ok = false; break; }
+      tc_fence_after();
+      const float inv = l_run > 0.0f ? 1.0f / l_run : 0.0f;
+      __half* dst = p.ctx + ((size_t)it.b * p.S + qrow) * p.d_model + (size_t)it.h * HD;
+      const bool store = qrow < p.S;
+#pragma unroll
+      for (int c = 0; c < HD / 32; ++c) {
+        uint32_t o[32];
+        tmem_ld32(o_col + c * 32, o);
+        tmem_ld_wait();
+        if (store) {
+#pragma unroll
+          for (int i2 = 0; i2 < 32; i2 += 8) {
+            uint4 w;
+            w.x = pack_half2(__uint_as_float(o[i2]) * inv, __uint_as_float(o[i2 + 1]) * inv);
+            w.y = pack_half2(__uint_as_float(o[i2 + 2]) * inv, __uint_as_float(o[i2 + 3]) * inv);
+            w.z = pack_half2(__uint_as_float(o[i2 + 4]) * inv, __uint_as_float(o[i2 + 5]) * inv);
+            w.w = pack_half2(__uint_as_float(o[i2 + 6]) * inv, __uint_as_float(o[i2 + 7]) * inv);
+            *reinterpret_cast<uint4*>(dst + c * 32 + i2) = w;
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(o_free + t);  // O_t may be overwritten by the next item
+      cs += nkv_t;
+      ++ci;
     }
   }
   tc_fence_before();

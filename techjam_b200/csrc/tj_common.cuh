@@ -257,4 +257,65 @@ TJ_DEV uint32_t pack_half2(float a, float b) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// sm_100 three-input max and packed two-lane FP32 arithmetic (one
+// instruction for two values; each lane rounds like its scalar form).
+TJ_DEV float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+TJ_DEV uint64_t f32x2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+TJ_DEV float2 f32x2_split(uint64_t v) {
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+  return r;
+}
+TJ_DEV uint64_t ffma_x2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+TJ_DEV uint64_t fadd_x2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// Max of one 128-column score row (8 independent three-input chains).
+TJ_DEV float row_max128(const uint32_t (&s)[128]) {
+  float m[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) m[k] = fmaxf(__uint_as_float(s[2 * k]), __uint_as_float(s[2 * k + 1]));
+#pragma unroll
+  for (int i = 16; i < 128; i += 16)
+#pragma unroll
+    for (int k = 0; k < 8; ++k) m[k] = max3f(m[k], __uint_as_float(s[i + 2 * k]), __uint_as_float(s[i + 2 * k + 1]));
+  return max3f(max3f(m[0], m[1], m[2]), max3f(m[3], m[4], m[5]), fmaxf(m[6], m[7]));
+}
+
+// P = 2^(S * sl2 - msub) for one 128-column row: packed to fp16 pairs in
+// place (word i from columns 2i, 2i+1, both >= i) and summed in FP32.
+TJ_DEV float exp_pack_rowsum(uint32_t (&s)[128], float sl2, float msub) {
+  const uint64_t scale2 = f32x2(sl2, sl2);
+  const uint64_t neg2 = f32x2(-msub, -msub);
+  uint64_t acc[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) acc[k] = 0ull;
+#pragma unroll
+  for (int i = 0; i < 64; ++i) {
+    const float2 x = f32x2_split(ffma_x2(f32x2(__uint_as_float(s[2 * i]), __uint_as_float(s[2 * i + 1])), scale2,
+                                         neg2));
+    const float p0 = fast_exp2(x.x);
+    const float p1 = fast_exp2(x.y);
+    acc[i & 3] = fadd_x2(acc[i & 3], f32x2(p0, p1));
+    s[i] = pack_half2(p0, p1);
+  }
+  const float2 a = f32x2_split(fadd_x2(fadd_x2(acc[0], acc[1]), fadd_x2(acc[2], acc[3])));
+  return a.x + a.y;
+}
+
 }  // namespace tj
