@@ -42,6 +42,12 @@ struct GemmParams {
 constexpr int kGemmBM = 128;
 constexpr int kGemmBK = 64;  // one 128-byte swizzle atom of fp16
 
+// Residual-epilogue staging: per epilogue warp 16 rows x 36 floats (32 + 4
+// padding, so both the row-per-lane writes and the column-per-lane reads of
+// 16-byte words are bank-conflict free).
+constexpr int kEpiStageFloats = 16 * 36;
+constexpr int kEpiStageBytes = 8 * kEpiStageFloats * 4;
+
 template <int BN>
 struct GemmCfg {
   static constexpr int kStageA = kGemmBM * kGemmBK * 2;
@@ -49,7 +55,7 @@ struct GemmCfg {
   static constexpr int kStageBytes = kStageA + kStageB;
   static constexpr int kStages = (200 * 1024) / kStageBytes;
   static constexpr int kTmemCols = 2 * BN;  // double-buffered accumulator
-  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/ + kEpiStageBytes;
   static constexpr int kThreads = 320;  // TMA warp, MMA warp, 8 epilogue warps
   static constexpr int kEpiThreads = 256;
 };
@@ -86,6 +92,80 @@ TJ_DEV float gelu_erf(float x) {
 struct ChunkOperands {
   float4 resid[8];
 };
+
+// FP32 residual epilogue of one epilogue warp: its 32 accumulator rows x
+// kChunks 32-column chunks (TMEM lane = row, one row per thread).  Each chunk
+// is turned to a column-per-lane layout through shared memory (two rounds of
+// 16 rows), so every global load of the residual and store of the result
+// moves whole 128-byte lines (lane l: row 4i + l/8, columns 4(l%8)..+3); the
+// next chunk's residual is loaded while the current one is stored.  Rows
+// outside a sample's valid length are written as zeros, rows >= M not at all.
+template <int kChunks, typename WaitAcc>
+TJ_DEV bool resid_epilogue(const GemmParams& p, uint32_t taddr, int row0, int colh, bool live, float* stage,
+                           int lane, WaitAcc&& wait_acc) {
+  const int sub = lane >> 3;
+  const int c4 = 4 * (lane & 7);
+  uint32_t in_m = 0, valid = 0;  // bit i: row row0 + 4i + sub is < M / valid
+  if (live) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int row = row0 + 4 * i + sub;
+      if (row < p.M) {
+        in_m |= 1u << i;
+        if (row_is_valid(p, row)) valid |= 1u << i;
+      }
+    }
+  }
+  float4 res[2][8];
+  auto prefetch = [&](int c, float4 (&r)[8]) {
+    const int col = colh + c * 32 + c4;
+    if (colh + c * 32 >= p.N) return;
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if ((valid >> i) & 1u) r[i] = *reinterpret_cast<const float4*>(p.resid + (size_t)(row0 + 4 * i + sub) * p.N + col);
+  };
+  if (live) prefetch(0, res[0]);  // overlaps the tile's last MMAs
+  if (!wait_acc()) return false;
+  tc_fence_after();
+#pragma unroll
+  for (int c = 0; c < kChunks; ++c) {
+    if (live && c + 1 < kChunks) prefetch(c + 1, res[(c + 1) & 1]);
+    uint32_t acc[32];
+    tmem_ld32(taddr + c * 32, acc);
+    tmem_ld_wait();
+    const int col0 = colh + c * 32;
+    if (!live || col0 >= p.N) continue;  // warp-uniform
+    const float4 b4 = __ldg(reinterpret_cast<const float4*>(p.bias + col0 + c4));
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      if ((lane >> 4) == h) {
+        float* dst = stage + (lane - 16 * h) * 36;
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          *reinterpret_cast<float4*>(dst + 4 * k) =
+              make_float4(__uint_as_float(acc[4 * k]), __uint_as_float(acc[4 * k + 1]),
+                          __uint_as_float(acc[4 * k + 2]), __uint_as_float(acc[4 * k + 3]));
+      }
+      __syncwarp();
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int ii = 4 * h + i;
+        const int rr = 4 * i + sub;
+        if ((in_m >> ii) & 1u) {
+          const float4 a = *reinterpret_cast<const float4*>(stage + rr * 36 + c4);
+          float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+          if ((valid >> ii) & 1u) {
+            const float4 r = res[c & 1][ii];
+            o = make_float4(a.x + b4.x + r.x, a.y + b4.y + r.y, a.z + b4.z + r.z, a.w + b4.w + r.w);
+          }
+          *reinterpret_cast<float4*>(p.out32 + (size_t)(row0 + 16 * h + rr) * p.N + col0 + c4) = o;
+        }
+      }
+      __syncwarp();
+    }
+  }
+  return true;
+}
 
 template <int EPI>
 TJ_DEV void load_chunk_operands(const GemmParams& p, int row, bool valid, int col0, ChunkOperands& o) {
@@ -173,6 +253,8 @@ __global__ void __launch_bounds__(320, 1)
   uint64_t* acc_full = bars + 2 * S; // [2]
   uint64_t* acc_empty = acc_full + 2;// [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  float* stage = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + 256) +
+                 (threadIdx.x / 32 - 2) * kEpiStageFloats;  // epilogue warps 2..9
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -260,12 +342,21 @@ __global__ void __launch_bounds__(320, 1)
       const bool in_range = row < p.M;
       const bool valid = row_is_valid(p, row);
       const int colh = nt * BN + half * (BN / 2);
+      const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + abuf * BN + half * (BN / 2);
+      if constexpr (EPI == kEpiResid) {
+        if (!resid_epilogue<kChunks>(p, taddr, mt * kGemmBM + quarter * 32, colh, true, stage, lane,
+                                     [&] { return mbar_wait(acc_full + abuf, aphase, p.err, kErrGemmEpilogue); }))
+          break;
+        tc_fence_before();
+        mbar_arrive(acc_empty + abuf);
+        if (++abuf == 2) { abuf = 0; aphase ^= 1u; }
+        continue;
+      }
       // operands of the first chunk are fetched while the MMAs still run
       ChunkOperands ops[2];
       if (in_range && colh < p.N) load_chunk_operands<EPI>(p, row, valid, colh, ops[0]);
       if (!mbar_wait(acc_full + abuf, aphase, p.err, kErrGemmEpilogue)) break;
       tc_fence_after();
-      const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + abuf * BN + half * (BN / 2);
 #pragma unroll
       for (int c = 0; c < kChunks; ++c) {
         const int col0 = colh + c * 32;
@@ -303,7 +394,7 @@ struct Gemm2Cfg {
   static constexpr int kStageBytes = 2 * kGemmBM * kGemmBK * 2;  // A 16 KB + W half 16 KB
   static constexpr int kStages = 6;
   static constexpr int kTmemCols = 512;                 // 2 x 256-column accumulators
-  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 256;
+  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 256 + kEpiStageBytes;
   static constexpr int kThreads = 320;
   static constexpr int kEpiThreads = 256;
 };
@@ -323,6 +414,8 @@ __global__ void __launch_bounds__(320, 1)
   uint64_t* acc_full = bars + 2 * S;  // [2]
   uint64_t* acc_empty = acc_full + 2; // [2] (even CTA's copy is the live one)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  float* stage = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + 256) +
+                 (threadIdx.x / 32 - 2) * kEpiStageFloats;  // epilogue warps 2..9
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -424,11 +517,20 @@ __global__ void __launch_bounds__(320, 1)
       const bool in_range = !ghost && row < p.M;
       const bool valid = in_range && row_is_valid(p, row);
       const int colh = nt * BN + half * (BN / 2);
+      const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + abuf * BN + half * (BN / 2);
+      if constexpr (EPI == kEpiResid) {
+        if (!resid_epilogue<kChunks>(p, taddr, mt * kGemmBM + quarter * 32, colh, !ghost, stage, lane,
+                                     [&] { return mbar_wait(acc_full + abuf, aphase, p.err, kErrGemmEpilogue); }))
+          break;
+        tc_fence_before();
+        mbar_arrive_cluster(leader_acc_empty0 + (uint32_t)(abuf * sizeof(uint64_t)));
+        if (++abuf == 2) { abuf = 0; aphase ^= 1u; }
+        continue;
+      }
       ChunkOperands ops[2];
       if (in_range) load_chunk_operands<EPI>(p, row, valid, colh, ops[0]);
       if (!mbar_wait(acc_full + abuf, aphase, p.err, kErrGemmEpilogue)) break;
       tc_fence_after();
-      const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + abuf * BN + half * (BN / 2);
 #pragma unroll
       for (int c = 0; c < kChunks; ++c) {
         const int col0 = colh + c * 32;
