@@ -5,10 +5,11 @@
 // One CTA per SM.  Warp 0 issues TMA loads into a STAGES-deep shared-memory
 // ring, warp 1 (one thread) issues tcgen05.mma into one of two TMEM
 // accumulators, warps 2..9 drain the other accumulator through the epilogue
-// (tcgen05.ld -> bias / GELU / residual / head scatter -> global).  Two
-// epilogue warps share each TMEM lane quarter, one per half of the tile's
-// columns, and each prefetches the next 32-column chunk's residual while the
-// current chunk is computed.  M tiles that hold no valid token (right
+// (tcgen05.ld -> bias / GELU / residual / head scatter -> shared-memory
+// transpose -> whole-line global stores).  Two epilogue warps share each TMEM
+// lane quarter, one per half of the tile's columns; the residual epilogue
+// prefetches the next 32-column chunk's residual while the current chunk is
+// stored.  M tiles that hold no valid token (right
 // padding) are dropped up front: the kernel walks a compact device-side list
 // of live 128-row tiles.
 #pragma once
@@ -42,9 +43,10 @@ struct GemmParams {
 constexpr int kGemmBM = 128;
 constexpr int kGemmBK = 64;  // one 128-byte swizzle atom of fp16
 
-// Residual-epilogue staging: per epilogue warp 16 rows x 36 floats (32 + 4
-// padding, so both the row-per-lane writes and the column-per-lane reads of
-// 16-byte words are bank-conflict free).
+// Epilogue staging: per epilogue warp 16 rows x 36 floats (FP32 residual
+// epilogue: 32 + 4 padding, so both the row-per-lane writes and the
+// column-per-lane reads of 16-byte words are bank-conflict free; the fp16
+// epilogues use 16 rows x 80 bytes of it).
 constexpr int kEpiStageFloats = 16 * 36;
 constexpr int kEpiStageBytes = 8 * kEpiStageFloats * 4;
 
@@ -87,11 +89,93 @@ TJ_DEV float gelu_erf(float x) {
   return 0.5f * x * (x >= 0.0f ? 2.0f - pe : pe);
 }
 
-// DRAM operand of an epilogue chunk (one row x 32 columns): the residual.
-// (The bias row is shared by every row of the tile and stays L1-resident.)
-struct ChunkOperands {
-  float4 resid[8];
-};
+// fp16 epilogue (bias, then GELU or nothing; QKV scatter or row-major
+// store) of one epilogue warp's 32 rows x kChunks 32-column chunks.  Each
+// chunk's packed 64-byte row pieces go through shared memory (two rounds of
+// 16 rows, 80-byte row pitch) so that each global store instruction writes
+// eight rows' 64-byte pieces whole (lane l: row 8i + l/4, bytes 16(l%4)..+15)
+// instead of 16 bytes in each of 32 rows.  Rows outside a sample's valid
+// length are written as zeros, rows >= M not at all.
+template <int EPI, int kChunks, typename WaitAcc>
+TJ_DEV bool f16_epilogue(const GemmParams& p, uint32_t taddr, int row0, int colh, bool live, float* stage_f,
+                         int lane, WaitAcc&& wait_acc) {
+  uint8_t* stage = reinterpret_cast<uint8_t*>(stage_f);
+  const bool my_valid = live && row_is_valid(p, row0 + lane);  // this thread's accumulator row
+  const int piece = lane & 3;
+  uint32_t in_m = 0;  // bit 2h+i: store-side row row0 + 16h + 8i + lane/4 is < M
+  if (live) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      if (row0 + 8 * k + (lane >> 2) < p.M) in_m |= 1u << k;
+  }
+  if (!wait_acc()) return false;
+  tc_fence_after();
+#pragma unroll
+  for (int c = 0; c < kChunks; ++c) {
+    uint32_t acc[32];
+    tmem_ld32(taddr + c * 32, acc);
+    tmem_ld_wait();
+    const int col0 = colh + c * 32;
+    if (!live || col0 >= p.N) continue;  // warp-uniform
+    uint32_t w[16];
+    if (my_valid) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float4 bb = __ldg(reinterpret_cast<const float4*>(p.bias + col0) + j);
+        float v0 = __uint_as_float(acc[4 * j]) + bb.x, v1 = __uint_as_float(acc[4 * j + 1]) + bb.y;
+        float v2 = __uint_as_float(acc[4 * j + 2]) + bb.z, v3 = __uint_as_float(acc[4 * j + 3]) + bb.w;
+        if constexpr (EPI == kEpiGelu) {
+          v0 = gelu_erf(v0); v1 = gelu_erf(v1); v2 = gelu_erf(v2); v3 = gelu_erf(v3);
+        }
+        w[2 * j] = pack_half2(v0, v1);
+        w[2 * j + 1] = pack_half2(v2, v3);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) w[j] = 0u;
+    }
+    // column part of the destination (a 32-column chunk never straddles a head)
+    __half* col_base;
+    int which = 0, head = 0, dim0 = 0;
+    if constexpr (EPI == kEpiQKV) {
+      which = col0 / p.d_model;
+      const int hc = col0 - which * p.d_model;
+      head = hc / p.head_dim;
+      dim0 = hc - head * p.head_dim;
+      col_base = which == 0 ? p.q : (which == 1 ? p.k : p.v);
+    } else {
+      col_base = p.out16 + col0;
+    }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      if ((lane >> 4) == h) {
+        uint4* dst = reinterpret_cast<uint4*>(stage + (lane - 16 * h) * 80);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) dst[k] = make_uint4(w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
+      }
+      __syncwarp();
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const int rr = 8 * i + (lane >> 2);
+        if ((in_m >> (2 * h + i)) & 1u) {
+          const uint4 val = *reinterpret_cast<const uint4*>(stage + rr * 80 + 16 * piece);
+          const int row = row0 + 16 * h + rr;
+          __half* dst;
+          if constexpr (EPI == kEpiQKV) {
+            const int b = row / p.seq;
+            const int n = row - b * p.seq;
+            dst = col_base + (((size_t)b * p.heads + head) * p.seq + n) * p.head_dim + dim0;
+          } else {
+            dst = col_base + (size_t)row * p.N;
+          }
+          *reinterpret_cast<uint4*>(dst + 8 * piece) = val;
+        }
+      }
+      __syncwarp();
+    }
+  }
+  return true;
+}
 
 // FP32 residual epilogue of one epilogue warp: its 32 accumulator rows x
 // kChunks 32-column chunks (TMEM lane = row, one row per thread).  Each chunk
@@ -165,78 +249,6 @@ TJ_DEV bool resid_epilogue(const GemmParams& p, uint32_t taddr, int row0, int co
     }
   }
   return true;
-}
-
-template <int EPI>
-TJ_DEV void load_chunk_operands(const GemmParams& p, int row, bool valid, int col0, ChunkOperands& o) {
-  if constexpr (EPI == kEpiResid) {
-    if (valid) {
-      const float4* src = reinterpret_cast<const float4*>(p.resid + (size_t)row * p.N + col0);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) o.resid[j] = src[j];
-    }
-  }
-}
-
-template <int EPI>
-TJ_DEV void epilogue_chunk(const GemmParams& p, int row, bool valid, int col0, const uint32_t (&acc)[32],
-                           const ChunkOperands& o) {
-  float v[32];
-  if (valid) {
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float4 bb = __ldg(reinterpret_cast<const float4*>(p.bias + col0) + j);
-      v[4 * j] = __uint_as_float(acc[4 * j]) + bb.x;
-      v[4 * j + 1] = __uint_as_float(acc[4 * j + 1]) + bb.y;
-      v[4 * j + 2] = __uint_as_float(acc[4 * j + 2]) + bb.z;
-      v[4 * j + 3] = __uint_as_float(acc[4 * j + 3]) + bb.w;
-    }
-  } else {
-#pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = 0.0f;
-  }
-  if constexpr (EPI == kEpiResid) {
-    float* dst = p.out32 + (size_t)row * p.N + col0;
-    if (valid) {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        v[4 * j] += o.resid[j].x; v[4 * j + 1] += o.resid[j].y;
-        v[4 * j + 2] += o.resid[j].z; v[4 * j + 3] += o.resid[j].w;
-      }
-    }
-#pragma unroll
-    for (int j = 0; j < 32; j += 4)
-      *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-  } else {
-    if constexpr (EPI == kEpiGelu) {
-      if (valid) {
-#pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = gelu_erf(v[j]);
-      }
-    }
-    __half* dst;
-    if constexpr (EPI == kEpiQKV) {
-      const int which = col0 / p.d_model;
-      const int hc = col0 - which * p.d_model;
-      const int head = hc / p.head_dim;
-      const int dim0 = hc - head * p.head_dim;
-      const int b = row / p.seq;
-      const int n = row - b * p.seq;
-      __half* base = which == 0 ? p.q : (which == 1 ? p.k : p.v);
-      dst = base + (((size_t)b * p.heads + head) * p.seq + n) * p.head_dim + dim0;
-    } else {
-      dst = p.out16 + (size_t)row * p.N + col0;
-    }
-#pragma unroll
-    for (int j = 0; j < 32; j += 8) {
-      uint4 w;
-      w.x = pack_half2(v[j], v[j + 1]);
-      w.y = pack_half2(v[j + 2], v[j + 3]);
-      w.z = pack_half2(v[j + 4], v[j + 5]);
-      w.w = pack_half2(v[j + 6], v[j + 7]);
-      *reinterpret_cast<uint4*>(dst + j) = w;
-    }
-  }
 }
 
 template <int BN, int EPI>
@@ -332,41 +344,21 @@ __global__ void __launch_bounds__(320, 1)
     const int quarter = warp & 3;         // TMEM lane quarter this warp may access
     const int half = (warp - 2) >> 2;     // which half of the tile's columns
     constexpr int kChunks = BN / 64;      // 32-column chunks per half
-    const int row_in_tile = quarter * 32 + lane;
     int abuf = 0;
     uint32_t aphase = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
       const int mt = __ldg(p.tile_list + t / n_tiles);
       const int nt = t % n_tiles;
-      const int row = mt * kGemmBM + row_in_tile;
-      const bool in_range = row < p.M;
-      const bool valid = row_is_valid(p, row);
+      const int row0 = mt * kGemmBM + quarter * 32;
       const int colh = nt * BN + half * (BN / 2);
       const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + abuf * BN + half * (BN / 2);
-      if constexpr (EPI == kEpiResid) {
-        if (!resid_epilogue<kChunks>(p, taddr, mt * kGemmBM + quarter * 32, colh, true, stage, lane,
-                                     [&] { return mbar_wait(acc_full + abuf, aphase, p.err, kErrGemmEpilogue); }))
-          break;
-        tc_fence_before();
-        mbar_arrive(acc_empty + abuf);
-        if (++abuf == 2) { abuf = 0; aphase ^= 1u; }
-        continue;
-      }
-      // operands of the first chunk are fetched while the MMAs still run
-      ChunkOperands ops[2];
-      if (in_range && colh < p.N) load_chunk_operands<EPI>(p, row, valid, colh, ops[0]);
-      if (!mbar_wait(acc_full + abuf, aphase, p.err, kErrGemmEpilogue)) break;
-      tc_fence_after();
-#pragma unroll
-      for (int c = 0; c < kChunks; ++c) {
-        const int col0 = colh + c * 32;
-        if (c + 1 < kChunks && in_range && col0 + 32 < p.N)
-          load_chunk_operands<EPI>(p, row, valid, col0 + 32, ops[(c + 1) & 1]);
-        uint32_t acc[32];
-        tmem_ld32(taddr + c * 32, acc);
-        tmem_ld_wait();
-        if (in_range && col0 < p.N) epilogue_chunk<EPI>(p, row, valid, col0, acc, ops[c & 1]);
-      }
+      auto wait_acc = [&] { return mbar_wait(acc_full + abuf, aphase, p.err, kErrGemmEpilogue); };
+      bool ok;
+      if constexpr (EPI == kEpiResid)
+        ok = resid_epilogue<kChunks>(p, taddr, row0, colh, true, stage, lane, wait_acc);
+      else
+        ok = f16_epilogue<EPI, kChunks>(p, taddr, row0, colh, true, stage, lane, wait_acc);
+      if (!ok) break;
       tc_fence_before();
       mbar_arrive(acc_empty + abuf);
       if (++abuf == 2) { abuf = 0; aphase ^= 1u; }
@@ -505,7 +497,6 @@ __global__ void __launch_bounds__(320, 1)
     const int quarter = warp & 3;
     const int half = (warp - 2) >> 2;
     constexpr int kChunks = BN / 64;
-    const int row_in_tile = quarter * 32 + lane;
     const uint32_t leader_acc_empty0 = map_to_rank(acc_empty, 0);
     int abuf = 0;
     uint32_t aphase = 0;
@@ -513,33 +504,16 @@ __global__ void __launch_bounds__(320, 1)
       bool ghost;
       const int mt = my_mtile(t, ghost);
       const int nt = t % n_tiles;
-      const int row = mt * kGemmBM + row_in_tile;
-      const bool in_range = !ghost && row < p.M;
-      const bool valid = in_range && row_is_valid(p, row);
+      const int row0 = mt * kGemmBM + quarter * 32;
       const int colh = nt * BN + half * (BN / 2);
       const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + abuf * BN + half * (BN / 2);
-      if constexpr (EPI == kEpiResid) {
-        if (!resid_epilogue<kChunks>(p, taddr, mt * kGemmBM + quarter * 32, colh, !ghost, stage, lane,
-                                     [&] { return mbar_wait(acc_full + abuf, aphase, p.err, kErrGemmEpilogue); }))
-          break;
-        tc_fence_before();
-        mbar_arrive_cluster(leader_acc_empty0 + (uint32_t)(abuf * sizeof(uint64_t)));
-        if (++abuf == 2) { abuf = 0; aphase ^= 1u; }
-        continue;
-      }
-      ChunkOperands ops[2];
-      if (in_range) load_chunk_operands<EPI>(p, row, valid, colh, ops[0]);
-      if (!mbar_wait(acc_full + abuf, aphase, p.err, kErrGemmEpilogue)) break;
-      tc_fence_after();
-#pragma unroll
-      for (int c = 0; c < kChunks; ++c) {
-        const int col0 = colh + c * 32;
-        if (c + 1 < kChunks && in_range) load_chunk_operands<EPI>(p, row, valid, col0 + 32, ops[(c + 1) & 1]);
-        uint32_t acc[32];
-        tmem_ld32(taddr + c * 32, acc);
-        tmem_ld_wait();
-        if (in_range) epilogue_chunk<EPI>(p, row, valid, col0, acc, ops[c & 1]);
-      }
+      auto wait_acc = [&] { return mbar_wait(acc_full + abuf, aphase, p.err, kErrGemmEpilogue); };
+      bool ok;
+      if constexpr (EPI == kEpiResid)
+        ok = resid_epilogue<kChunks>(p, taddr, row0, colh, !ghost, stage, lane, wait_acc);
+      else
+        ok = f16_epilogue<EPI, kChunks>(p, taddr, row0, colh, !ghost, stage, lane, wait_acc);
+      if (!ok) break;
       tc_fence_before();
       mbar_arrive_cluster(leader_acc_empty0 + (uint32_t)(abuf * sizeof(uint64_t)));
       if (++abuf == 2) { abuf = 0; aphase ^= 1u; }
