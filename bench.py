@@ -49,8 +49,13 @@ from techjam_b200.sharding import SeqShardComm, forward_seqshard, shard_samples,
 
 SEED = 1234 + 100000  # the reference harness's timing input seed (torch_transformer_benchmark.py:459-466)
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
-# DRAM bytes per launch from ncu captures (profiles/*.md), keyed (workload, kernel class).
-NCU_TRAFFIC_BYTES: dict = {}
+# dram__bytes_read.sum + dram__bytes_write.sum of one launch of the workload's dominant
+# kernel, from ncu captures of this build (profiles/*.md), keyed (workload, kernel class).
+NCU_TRAFFIC_BYTES: dict = {
+    ("C1", "attention"): 2632192 + 0,               # attn_fwd_persistent_kernel<32>
+    ("C2", "attention"): 141639936 + 29552896,      # attn_fwd_kernel<64>
+    ("C3", "gemm_ffn_in"): 57665792 + 168056064,    # gemm_tc_kernel<256,1>
+}
 CPU_DENSE_MAX = 8192  # longest sample the CPU baseline runs through the dense model
 
 
