@@ -279,34 +279,43 @@ TJ_DEV uint64_t ffma_x2(uint64_t a, uint64_t b, uint64_t c) {
   asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
   return d;
 }
+TJ_DEV uint64_t fmul_x2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
 TJ_DEV uint64_t fadd_x2(uint64_t a, uint64_t b) {
   uint64_t d;
   asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
 }
 
-// Max of one 128-column score row (8 independent three-input chains).
-TJ_DEV float row_max128(const uint32_t (&s)[128]) {
+// Max of one N-column score row (8 independent three-input chains).
+template <int N>
+TJ_DEV float row_max(const uint32_t (&s)[N]) {
+  static_assert(N % 16 == 0 && N >= 32, "row length");
   float m[8];
 #pragma unroll
   for (int k = 0; k < 8; ++k) m[k] = fmaxf(__uint_as_float(s[2 * k]), __uint_as_float(s[2 * k + 1]));
 #pragma unroll
-  for (int i = 16; i < 128; i += 16)
+  for (int i = 16; i < N; i += 16)
 #pragma unroll
     for (int k = 0; k < 8; ++k) m[k] = max3f(m[k], __uint_as_float(s[i + 2 * k]), __uint_as_float(s[i + 2 * k + 1]));
   return max3f(max3f(m[0], m[1], m[2]), max3f(m[3], m[4], m[5]), fmaxf(m[6], m[7]));
 }
+TJ_DEV float row_max128(const uint32_t (&s)[128]) { return row_max<128>(s); }
 
-// P = 2^(S * sl2 - msub) for one 128-column row: packed to fp16 pairs in
-// place (word i from columns 2i, 2i+1, both >= i) and summed in FP32.
-TJ_DEV float exp_pack_rowsum(uint32_t (&s)[128], float sl2, float msub) {
+// P = 2^(S * sl2 - msub) for one N-column row: packed to fp16 pairs in place
+// (word i from columns 2i, 2i+1, both >= i) and summed in FP32.
+template <int N>
+TJ_DEV float exp_pack_rowsum(uint32_t (&s)[N], float sl2, float msub) {
   const uint64_t scale2 = f32x2(sl2, sl2);
   const uint64_t neg2 = f32x2(-msub, -msub);
   uint64_t acc[4];
 #pragma unroll
   for (int k = 0; k < 4; ++k) acc[k] = 0ull;
 #pragma unroll
-  for (int i = 0; i < 64; ++i) {
+  for (int i = 0; i < N / 2; ++i) {
     const float2 x = f32x2_split(ffma_x2(f32x2(__uint_as_float(s[2 * i]), __uint_as_float(s[2 * i + 1])), scale2,
                                          neg2));
     const float p0 = fast_exp2(x.x);
@@ -317,5 +326,6 @@ TJ_DEV float exp_pack_rowsum(uint32_t (&s)[128], float sl2, float msub) {
   const float2 a = f32x2_split(fadd_x2(fadd_x2(acc[0], acc[1]), fadd_x2(acc[2], acc[3])));
   return a.x + a.y;
 }
+TJ_DEV float exp_pack_rowsum(uint32_t (&s)[128], float sl2, float msub) { return exp_pack_rowsum<128>(s, sl2, msub); }
 
 }  // namespace tj

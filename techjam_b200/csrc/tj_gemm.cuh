@@ -77,16 +77,23 @@ TJ_DEV bool row_is_valid(const GemmParams& p, int row) {
 // Two SFU ops (reciprocal, exp2) and ~12 FMAs, no branches; for x < 0 the
 // 1 + erf term is the series itself (no cancellation).  The resulting GELU is
 // within 5e-7 of the exact one, far below the fp16 rounding of the output.
-TJ_DEV float gelu_erf(float x) {
-  constexpr float kP = 0.3275911f;
-  constexpr float kA1 = 0.254829592f, kA2 = -0.284496736f, kA3 = 1.421413741f, kA4 = -1.453152027f,
-                  kA5 = 1.061405429f;
-  const float z = fabsf(x) * 0.70710678118654752440f;
-  float t;
-  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t) : "f"(fmaf(kP, z, 1.0f)));
-  const float poly = t * fmaf(t, fmaf(t, fmaf(t, fmaf(t, kA5, kA4), kA3), kA2), kA1);
-  const float pe = poly * fast_exp2(-(z * z) * 1.4426950408889634f);  // t-series * exp(-z^2)
-  return 0.5f * x * (x >= 0.0f ? 2.0f - pe : pe);
+// Evaluated for two values at once on packed two-lane FP32 instructions
+// (each lane rounds like the scalar operation; half the FMA/MUL issue slots).
+TJ_DEV float2 gelu_erf_x2(float x0, float x1) {
+  const uint64_t z = fmul_x2(f32x2(fabsf(x0), fabsf(x1)), f32x2(0.70710678118654752440f, 0.70710678118654752440f));
+  const float2 den = f32x2_split(ffma_x2(f32x2(0.3275911f, 0.3275911f), z, f32x2(1.0f, 1.0f)));
+  float t0, t1;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t0) : "f"(den.x));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t1) : "f"(den.y));
+  const uint64_t t = f32x2(t0, t1);
+  uint64_t q = ffma_x2(t, f32x2(1.061405429f, 1.061405429f), f32x2(-1.453152027f, -1.453152027f));
+  q = ffma_x2(t, q, f32x2(1.421413741f, 1.421413741f));
+  q = ffma_x2(t, q, f32x2(-0.284496736f, -0.284496736f));
+  q = ffma_x2(t, q, f32x2(0.254829592f, 0.254829592f));
+  const uint64_t poly = fmul_x2(t, q);
+  const float2 arg = f32x2_split(fmul_x2(fmul_x2(z, z), f32x2(-1.4426950408889634f, -1.4426950408889634f)));
+  const float2 pe = f32x2_split(fmul_x2(poly, f32x2(fast_exp2(arg.x), fast_exp2(arg.y))));
+  return make_float2(0.5f * x0 * (x0 >= 0.0f ? 2.0f - pe.x : pe.x), 0.5f * x1 * (x1 >= 0.0f ? 2.0f - pe.y : pe.y));
 }
 
 // fp16 epilogue (bias, then GELU or nothing; QKV scatter or row-major
@@ -125,7 +132,8 @@ TJ_DEV bool f16_epilogue(const GemmParams& p, uint32_t taddr, int row0, int colh
         float v0 = __uint_as_float(acc[4 * j]) + bb.x, v1 = __uint_as_float(acc[4 * j + 1]) + bb.y;
         float v2 = __uint_as_float(acc[4 * j + 2]) + bb.z, v3 = __uint_as_float(acc[4 * j + 3]) + bb.w;
         if constexpr (EPI == kEpiGelu) {
-          v0 = gelu_erf(v0); v1 = gelu_erf(v1); v2 = gelu_erf(v2); v3 = gelu_erf(v3);
+          const float2 g01 = gelu_erf_x2(v0, v1), g23 = gelu_erf_x2(v2, v3);
+          v0 = g01.x; v1 = g01.y; v2 = g23.x; v3 = g23.y;
         }
         w[2 * j] = pack_half2(v0, v1);
         w[2 * j + 1] = pack_half2(v2, v3);
@@ -199,6 +207,15 @@ TJ_DEV bool resid_epilogue(const GemmParams& p, uint32_t taddr, int row0, int co
         if (row_is_valid(p, row)) valid |= 1u << i;
       }
     }
+  }
+  // Pull this lane's row of the residual slice into L2 while the tile's MMAs
+  // still run (one bulk prefetch, no registers); the register loads below
+  // then wait on L2 rather than DRAM.  Only for short reductions (out-proj):
+  // with K = 4096 the tile's own operand stream gains more from the L2.
+  if (p.K <= 1024 && live && colh < p.N && row_is_valid(p, row0 + lane)) {
+    const float* src = p.resid + (size_t)(row0 + lane) * p.N + colh;
+    const int bytes = min(kChunks * 32, p.N - colh) * 4;
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
   }
   float4 res[2][8];
   auto prefetch = [&](int c, float4 (&r)[8]) {
