@@ -247,7 +247,7 @@ int launch_attn_hd(const void* q, const void* k, const void* v, const tj::AttnPa
       const long long items = (long long)n_pairs * B * p.H;
       if (items > 0x7fffffffLL - 2LL * di.sms) return fail(TJ_ERR_UNSUPPORTED, "too many attention work items");
       const int grid = (int)std::min<long long>(items, di.sms);
-      kern<<<grid, Cfg::kThreads, Cfg::kSmemPersist, st>>>(tq, tk, tv, p, n_pairs, (int)items);
+      kern<<<grid, Cfg::kThreadsPersist, Cfg::kSmemPersist, st>>>(tq, tk, tv, p, n_pairs, (int)items);
     }
   } else {
     static bool attr_set[64] = {};

@@ -71,12 +71,15 @@ struct AttnCfg {
   static constexpr int kColS = 0;
   static constexpr int kColP = kPSeparate ? 256 : 0;
   static constexpr int kColO = kPSeparate ? 384 : 256;
-  static constexpr int kThreads = 320;
+  // TMA warp 8, MMA warp 9, 8 softmax warps; with P in its own columns a
+  // second MMA warp (10) issues tile 1's S and PV.
+  static constexpr int kThreads = HD <= 64 ? 352 : 320;
+  static constexpr int kThreadsPersist = 320;
   static constexpr float kRescaleLog2 = 8.0f;
 };
 
 template <int HD>
-__global__ void __launch_bounds__(320, 1)
+__global__ void __launch_bounds__(AttnCfg<HD>::kThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
   using Cfg = AttnCfg<HD>;
@@ -119,7 +122,7 @@ __global__ void __launch_bounds__(320, 1)
   const int lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int i = 0; i < ST; ++i) { mbar_init(kv_full + i, 1); mbar_init(kv_empty + i, 1); }
+    for (int i = 0; i < ST; ++i) { mbar_init(kv_full + i, 1); mbar_init(kv_empty + i, Cfg::kPSeparate ? 2 : 1); }
     for (int i = 0; i < 2; ++i) {
       mbar_init(s_full + i, 1);
       mbar_init(p_full + i, 128);
@@ -169,9 +172,9 @@ __global__ void __launch_bounds__(320, 1)
         }
       }
     }
-  } else if (warp == 9) {
+  } else if (warp == 9 || (Cfg::kPSeparate && warp == 10)) {
     if (lane == 0) {
-      // ---------------------------------------------------------- MMA issuer
+      // ---------------------------------------------------------- MMA issuer(s)
       constexpr uint32_t idesc_qk = idesc_f16_f32(128, 128, false, false);
       constexpr uint32_t idesc_pv = idesc_f16_f32(128, HD, false, true);
       const uint32_t q_addr = smem_u32(sQ);
@@ -201,31 +204,34 @@ __global__ void __launch_bounds__(320, 1)
       };
       auto kv_addr = [&](int jj) { return smem_u32(sKV + (jj % ST) * 2 * Cfg::kTile); };
       if constexpr (Cfg::kPSeparate) {
-        // Lookahead order per step j: S_t(j+1) as soon as the softmax has read
-        // S_t(j), then PV_t(j) once P_t(j) is ready.
-        if (ok && (ok = mbar_wait(kv_full, 0, p.err, kErrAttnMma))) {
-          tc_fence_after();
-          for (int t = 0; t < 2; ++t)
-            if (0 < (t == 0 ? nkv0 : nkv1)) issue_s(t, 0, kv_addr(0));
-        }
+        // One issuing warp per query tile (warp 9: tile 0, warp 10: tile 1),
+        // so neither tile's S or PV waits behind the other tile's softmax.
+        // Per step j: S_t(j+1) as soon as the softmax has read S_t(j), then
+        // PV_t(j) once P_t(j) is ready.  Both issuers release every K/V stage
+        // (count 2): by a commit after their MMAs, or, for the steps past
+        // their tile's last key tile, by a plain arrive once the stage landed.
+        const int t = warp - 9;
+        const int nkv_t = t == 0 ? nkv0 : nkv1;
         for (int j = 0; j < n_kv && ok; ++j) {
-          if (j + 1 < n_kv) {
+          const int st = j % ST;
+          if (!mbar_wait(kv_full + st, (j / ST) & 1, p.err, kErrAttnMma)) { ok = false; break; }
+          tc_fence_after();
+          if (j >= nkv_t) {
+            mbar_arrive(kv_empty + st);
+            continue;
+          }
+          if (j == 0) issue_s(t, 0, kv_addr(0));
+          if (j + 1 < nkv_t) {
             const int sn = (j + 1) % ST;
             if (!mbar_wait(kv_full + sn, ((j + 1) / ST) & 1, p.err, kErrAttnMma)) { ok = false; break; }
-            for (int t = 0; t < 2 && ok; ++t) {
-              if (j + 1 >= (t == 0 ? nkv0 : nkv1)) continue;
-              if (!mbar_wait(s_free + t, j & 1, p.err, kErrAttnMma)) { ok = false; break; }
-              tc_fence_after();
-              issue_s(t, j + 1, kv_addr(j + 1));
-            }
-          }
-          for (int t = 0; t < 2 && ok; ++t) {
-            if (j >= (t == 0 ? nkv0 : nkv1)) continue;
-            if (!mbar_wait(p_full + t, j & 1, p.err, kErrAttnMma)) { ok = false; break; }
+            if (!mbar_wait(s_free + t, j & 1, p.err, kErrAttnMma)) { ok = false; break; }
             tc_fence_after();
-            issue_pv(t, j, kv_addr(j) + Cfg::kTile);
+            issue_s(t, j + 1, kv_addr(j + 1));
           }
-          umma_commit(kv_empty + j % ST);
+          if (!mbar_wait(p_full + t, j & 1, p.err, kErrAttnMma)) { ok = false; break; }
+          tc_fence_after();
+          issue_pv(t, j, kv_addr(j) + Cfg::kTile);
+          umma_commit(kv_empty + st);
         }
       } else {
         // P_t(j) lives in S_t's columns: S_t(j+1) must wait for PV_t(j).
