@@ -74,7 +74,7 @@ struct AttnCfg {
   // TMA warp 8, MMA warp 9, 8 softmax warps; with P in its own columns a
   // second MMA warp (10) issues tile 1's S and PV.
   static constexpr int kThreads = HD <= 64 ? 352 : 320;
-  static constexpr int kThreadsPersist = 320;
+  static constexpr int kThreadsPersist = 352;  // TMA warp 8, MMA warps 9-10, 8 softmax warps
   static constexpr float kRescaleLog2 = 8.0f;
 };
 
@@ -381,7 +381,7 @@ namespace tj {
 // Q and K/V stream in while the current one finishes, and every barrier phase
 // is tracked with running use counters across items.
 template <int HD>
-__global__ void __launch_bounds__(320, 1)
+__global__ void __launch_bounds__(AttnCfg<HD>::kThreadsPersist, 1)
     attn_fwd_persistent_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                                const __grid_constant__ CUtensorMap tmV, const AttnParams p, int n_pairs,
                                int n_items) {
@@ -416,8 +416,9 @@ __global__ void __launch_bounds__(320, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 2; ++i) { mbar_init(q_full + i, 1); mbar_init(q_empty + i, 1); }
-    for (int i = 0; i < ST; ++i) { mbar_init(kv_full + i, 1); mbar_init(kv_empty + i, 1); }
+    // Q buffers and K/V stages are released by both MMA issuers
+    for (int i = 0; i < 2; ++i) { mbar_init(q_full + i, 1); mbar_init(q_empty + i, 2); }
+    for (int i = 0; i < ST; ++i) { mbar_init(kv_full + i, 1); mbar_init(kv_empty + i, 2); }
     for (int i = 0; i < 2; ++i) {
       mbar_init(s_full + i, 1);
       mbar_init(s_free + i, 128);
@@ -500,82 +501,80 @@ __global__ void __launch_bounds__(320, 1)
         ++nitem;
       }
     }
-  } else if (warp == 9) {
+  } else if (warp == 9 || warp == 10) {
     if (lane == 0) {
-      // ---------------------------------------------------------- MMA issuer
+      // ---------------------------------------------------------- MMA issuers
+      // Warp 9 issues query tile 0's S and PV, warp 10 tile 1's, each over the
+      // same item sequence; both release every K/V stage and Q buffer (count
+      // 2), by a commit after their MMAs or, where their tile takes no part,
+      // by a plain arrive once the stage or buffer has landed.
       constexpr uint32_t idesc_qk = idesc_f16_f32(128, 128, false, false);
       constexpr uint32_t idesc_pv = idesc_f16_f32(128, HD, false, true);
+      const int t = warp - 9;
       int kvc = 0, nitem = 0;
-      int cs[2] = {0, 0};  // S_t computed so far
-      int ci[2] = {0, 0};  // items in which tile t took part so far
+      int cs = 0;  // S_t computed so far
+      int ci = 0;  // items in which tile t took part so far
       bool ok = true;
       for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x) {
         Item it;
         if (!decode(i, it)) continue;
         const int qb = nitem & 1;
-        const int nkv[2] = {it.nkv0, it.nkv1};
+        const int nkv_t = t == 0 ? it.nkv0 : it.nkv1;
         if (!mbar_wait(q_full + qb, (nitem >> 1) & 1, p.err, kErrAttnMma)) break;
-        const uint32_t q_addr = smem_u32(sQ + qb * 2 * Cfg::kTile);
+        const uint32_t q_addr = smem_u32(sQ + qb * 2 * Cfg::kTile) + t * Cfg::kTile;
         auto kv_addr = [&](int j) { return smem_u32(sKV + ((kvc + j) % ST) * 2 * Cfg::kTile); };
-        auto issue_s = [&](int t, uint32_t k_addr) {
-          const uint32_t qa = q_addr + t * Cfg::kTile;
+        auto issue_s = [&](uint32_t k_addr) {
 #pragma unroll
           for (int ks = 0; ks < HD / 16; ++ks) {
             const int atom = (ks * 16) / Cfg::kAtomCols;
             const int within = ((ks * 16) % Cfg::kAtomCols) * 2;
-            const uint64_t ad = smem_desc(qa + atom * Cfg::kAtomBytes + within, 16, 8 * Cfg::kRowB, Cfg::kSw);
+            const uint64_t ad = smem_desc(q_addr + atom * Cfg::kAtomBytes + within, 16, 8 * Cfg::kRowB, Cfg::kSw);
             const uint64_t bd = smem_desc(k_addr + atom * Cfg::kAtomBytes + within, 16, 8 * Cfg::kRowB, Cfg::kSw);
             umma_f16_ss(tmem + Cfg::kColS + t * 128, ad, bd, idesc_qk, ks != 0);
           }
           umma_commit(s_full + t);
         };
-        // first key tile: S_t(0) once the previous item's last S_t has been read
-        {
-          const int g = kvc;
-          if (!mbar_wait(kv_full + g % ST, (g / ST) & 1, p.err, kErrAttnMma)) break;
-          tc_fence_after();
-          for (int t = 0; t < 2 && ok; ++t) {
-            if (nkv[t] == 0) continue;
-            if (cs[t] > 0 && !mbar_wait(s_free + t, (cs[t] - 1) & 1, p.err, kErrAttnMma)) { ok = false; break; }
-            tc_fence_after();
-            issue_s(t, kv_addr(0));
-          }
-        }
         for (int j = 0; j < it.n_kv && ok; ++j) {
-          if (j + 1 < it.n_kv) {
-            const int g = kvc + j + 1;
-            if (!mbar_wait(kv_full + g % ST, (g / ST) & 1, p.err, kErrAttnMma)) { ok = false; break; }
-            for (int t = 0; t < 2 && ok; ++t) {
-              if (j + 1 >= nkv[t]) continue;
-              if (!mbar_wait(s_free + t, (cs[t] + j) & 1, p.err, kErrAttnMma)) { ok = false; break; }
-              tc_fence_after();
-              issue_s(t, kv_addr(j + 1));
-            }
+          const int g = kvc + j;
+          if (!mbar_wait(kv_full + g % ST, (g / ST) & 1, p.err, kErrAttnMma)) { ok = false; break; }
+          tc_fence_after();
+          if (j >= nkv_t) {
+            mbar_arrive(kv_empty + g % ST);
+            continue;
           }
-          for (int t = 0; t < 2 && ok; ++t) {
-            if (j >= nkv[t]) continue;
-            if (!mbar_wait(p_full + t, (cs[t] + j) & 1, p.err, kErrAttnMma)) { ok = false; break; }
-            if (j == 0 && ci[t] > 0 && !mbar_wait(o_free + t, (ci[t] - 1) & 1, p.err, kErrAttnMma)) { ok = false; break; }
+          if (j == 0) {  // S_t(0) once the previous item's last S_t has been read
+            if (cs > 0 && !mbar_wait(s_free + t, (cs - 1) & 1, p.err, kErrAttnMma)) { ok = false; break; }
             tc_fence_after();
-            const uint32_t o_tmem = tmem + Cfg::kColO + t * HD;
-            const uint32_t p_tmem = tmem + Cfg::kColP + t * 64;
-            const uint32_t v_addr = kv_addr(j) + Cfg::kTile;
-#pragma unroll
-            for (int ks = 0; ks < 8; ++ks) {
-              const uint64_t bd = smem_desc(v_addr + ks * 16 * Cfg::kRowB, Cfg::kAtomBytes, 8 * Cfg::kRowB, Cfg::kSw);
-              umma_f16_ts(o_tmem, p_tmem + ks * 8, bd, idesc_pv, (j | ks) != 0);
-            }
-            umma_commit(pv_done + t);
-            if (j == nkv[t] - 1) umma_commit(o_final + t);
+            issue_s(kv_addr(0));
           }
-          umma_commit(kv_empty + (kvc + j) % ST);
+          if (j + 1 < nkv_t) {
+            const int gn = g + 1;
+            if (!mbar_wait(kv_full + gn % ST, (gn / ST) & 1, p.err, kErrAttnMma)) { ok = false; break; }
+            if (!mbar_wait(s_free + t, (cs + j) & 1, p.err, kErrAttnMma)) { ok = false; break; }
+            tc_fence_after();
+            issue_s(kv_addr(j + 1));
+          }
+          if (!mbar_wait(p_full + t, (cs + j) & 1, p.err, kErrAttnMma)) { ok = false; break; }
+          if (j == 0 && ci > 0 && !mbar_wait(o_free + t, (ci - 1) & 1, p.err, kErrAttnMma)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t o_tmem = tmem + Cfg::kColO + t * HD;
+          const uint32_t p_tmem = tmem + Cfg::kColP + t * 64;
+          const uint32_t v_addr = kv_addr(j) + Cfg::kTile;
+#pragma unroll
+          for (int ks = 0; ks < 8; ++ks) {
+            const uint64_t bd = smem_desc(v_addr + ks * 16 * Cfg::kRowB, Cfg::kAtomBytes, 8 * Cfg::kRowB, Cfg::kSw);
+            umma_f16_ts(o_tmem, p_tmem + ks * 8, bd, idesc_pv, (j | ks) != 0);
+          }
+          umma_commit(pv_done + t);
+          if (j == nkv_t - 1) umma_commit(o_final + t);
+          umma_commit(kv_empty + g % ST);
         }
-        umma_commit(q_empty + qb);
+        if (!ok) break;
+        if (nkv_t > 0) umma_commit(q_empty + qb);  // after this tile's S MMAs read Q
+        else mbar_arrive(q_empty + qb);
         kvc += it.n_kv;
-        for (int t = 0; t < 2; ++t) {
-          cs[t] += nkv[t];
-          ci[t] += nkv[t] > 0 ? 1 : 0;
-        }
+        cs += nkv_t;
+        ci += nkv_t > 0 ? 1 : 0;
         ++nitem;
       }
     }
