@@ -78,6 +78,20 @@ struct AttnCfg {
   static constexpr float kRescaleLog2 = 8.0f;
 };
 
+// Score-row masking (one thread = one query row of 128 key columns).
+// Columns past `lim` (future keys on the diagonal tile, keys past the valid
+// length on the tail tile) become -inf: a compare-and-select per column with
+// no other live state, so the 128 scores stay in registers.
+TJ_DEV void mask_past(uint32_t (&s)[128], int lim) {
+#pragma unroll
+  for (int i = 0; i < 128; ++i) s[i] = i > lim ? 0xff800000u : s[i];
+}
+// Columns whose key is masked out (general, non-prefix masks only).
+TJ_DEV void mask_keys(uint32_t (&s)[128], const uint8_t* __restrict__ key_valid) {
+#pragma unroll
+  for (int i = 0; i < 128; ++i) s[i] = __ldg(key_valid + i) == 0 ? 0xff800000u : s[i];
+}
+
 template <int HD>
 __global__ void __launch_bounds__(AttnCfg<HD>::kThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -288,17 +302,12 @@ __global__ void __launch_bounds__(AttnCfg<HD>::kThreads, 1)
       const int kbase = j * 128;
       const bool diag = p.causal && j == qg0 + t;
       const bool tail = kbase + 128 > len;
-      if (diag || tail || general) {
+      if (diag || tail) {
         const int lim_causal = diag ? r : 127;           // keys with col > lim are in the future
         const int lim_len = len - kbase - 1;             // keys with col > lim are past the length
-        const int lim = lim_causal < lim_len ? lim_causal : lim_len;
-#pragma unroll
-        for (int i = 0; i < 128; ++i) {
-          bool dead = i > lim;
-          if (kmask) dead = dead || (kmask[kbase + i] == 0);
-          if (dead) s[i] = __float_as_uint(-INFINITY);
-        }
+        mask_past(s, lim_causal < lim_len ? lim_causal : lim_len);
       }
+      if (general) mask_keys(s, kmask + kbase);
       const float mx = row_max128(s);
       const float m_tile = mx * sl2;
       const bool grow = m_tile > m_run + Cfg::kRescaleLog2;
@@ -614,17 +623,12 @@ __global__ void __launch_bounds__(AttnCfg<HD>::kThreadsPersist, 1)
         const int kbase = j * 128;
         const bool diag = p.causal && j == it.qg0 + t;
         const bool tail = kbase + 128 > it.len;
-        if (diag || tail || kmask) {
+        if (diag || tail) {
           const int lim_causal = diag ? r : 127;
           const int lim_len = it.len - kbase - 1;
-          const int lim = lim_causal < lim_len ? lim_causal : lim_len;
-#pragma unroll
-          for (int i2 = 0; i2 < 128; ++i2) {
-            bool dead = i2 > lim;
-            if (kmask) dead = dead || (kmask[kbase + i2] == 0);
-            if (dead) s[i2] = __float_as_uint(-INFINITY);
-          }
+          mask_past(s, lim_causal < lim_len ? lim_causal : lim_len);
         }
+        if (kmask) mask_keys(s, kmask + kbase);
         const float mx = row_max128(s);
         const float m_tile = mx * sl2;
         const bool grow = m_tile > m_run + Cfg::kRescaleLog2;
