@@ -164,18 +164,13 @@ __global__ void poly_guard_finalize(PolyParams p) {
 // chunk c of row r at c ^ (r & 7)).  The same bytes serve as the K-major A
 // operand of the apply GEMM (M = tokens, K = features) and as the MN-major A
 // operand of the update GEMM (M = features, K = tokens).
-TJ_DEV void load_row64(const uint8_t* tile, int row, float (&x)[64]) {
+// Row `row` of a [128 x 64] fp16 tile (128-byte swizzle) as 32 packed halves pairs.
+TJ_DEV void load_row_h2(const uint8_t* tile, int row, uint32_t (&h)[32]) {
   const uint8_t* base = tile + row * 128;
 #pragma unroll
   for (int c = 0; c < 8; ++c) {
     const uint4 w = *reinterpret_cast<const uint4*>(base + ((c ^ (row & 7)) << 4));
-    const __half2* h = reinterpret_cast<const __half2*>(&w);
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float2 f = __half22float2(h[e]);
-      x[c * 8 + 2 * e] = f.x;
-      x[c * 8 + 2 * e + 1] = f.y;
-    }
+    h[4 * c] = w.x; h[4 * c + 1] = w.y; h[4 * c + 2] = w.z; h[4 * c + 3] = w.w;
   }
 }
 
@@ -185,17 +180,20 @@ TJ_DEV float2 load_pair(const uint8_t* tile, int row, int i) {
   return __half22float2(*reinterpret_cast<const __half2*>(a));
 }
 
-// One atom row: feature j = coef * x[j] (j = 0..63).
-TJ_DEV void store_atom_row(uint8_t* atom, int row, float coef, const float (&x)[64]) {
+// One atom row: feature j = coef * x[j] (j = 0..63), as packed fp16
+// multiplies (coef rounded to fp16 once; for the key side's quadratic block
+// coef = k_i / 8 is exact, so those features are the correctly rounded
+// products).
+TJ_DEV void store_atom_row_h2(uint8_t* atom, int row, float coef, const uint32_t (&h)[32]) {
+  const __half2 c2 = __float2half2_rn(coef);
+  const uint32_t cw = *reinterpret_cast<const uint32_t*>(&c2);
   uint8_t* base = atom + row * 128;
 #pragma unroll
   for (int c = 0; c < 8; ++c) {
-    uint4 w;
-    w.x = pack_half2(coef * x[c * 8 + 0], coef * x[c * 8 + 1]);
-    w.y = pack_half2(coef * x[c * 8 + 2], coef * x[c * 8 + 3]);
-    w.z = pack_half2(coef * x[c * 8 + 4], coef * x[c * 8 + 5]);
-    w.w = pack_half2(coef * x[c * 8 + 6], coef * x[c * 8 + 7]);
-    *reinterpret_cast<uint4*>(base + ((c ^ (row & 7)) << 4)) = w;
+    uint32_t w[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(w[e]) : "r"(h[4 * c + e]), "r"(cw));
+    *reinterpret_cast<uint4*>(base + ((c ^ (row & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
   }
 }
 // One atom row holding a single constant in feature 0 (the phi0 slot), zeros elsewhere.
@@ -209,19 +207,16 @@ TJ_DEV void store_const_row(uint8_t* atom, int row, float c0) {
   }
 }
 
-// Writes feature block fb of this token row (x = the row, xi = elements
-// 2fb and 2fb+1 of it).  quad/lin/cst are the phi2, phi1 and phi0
-// coefficients (key side: scale, sqrt(scale), 1; query side folded with
-// c2, c1, c0).
-TJ_DEV void store_feature_block(uint8_t* tile, int row, int fb, const float (&x)[64], float2 xi, float quad,
-                                float lin, float cst) {
-  if (fb < 32) {
-    store_atom_row(tile, row, quad * xi.x, x);
-    store_atom_row(tile + 16384, row, quad * xi.y, x);
-  } else {
-    store_atom_row(tile, row, lin, x);
-    store_const_row(tile + 16384, row, cst);
-  }
+// Writes atom `a` (0: first, 1: second 64 features) of feature block fb of
+// this token row (h = the row, xi = its elements 2fb and 2fb+1).  quad/lin/cst
+// are the phi2, phi1 and phi0 coefficients (key side: scale, sqrt(scale), 1;
+// query side folded with c2, c1, c0).
+TJ_DEV void store_feature_atom(uint8_t* tile, int row, int fb, int a, const uint32_t (&h)[32], float2 xi,
+                               float quad, float lin, float cst) {
+  uint8_t* atom = tile + a * 16384;
+  if (fb < 32) store_atom_row_h2(atom, row, quad * (a == 0 ? xi.x : xi.y), h);
+  else if (a == 0) store_atom_row_h2(atom, row, lin, h);
+  else store_const_row(atom, row, cst);
 }
 
 // The constant B operand [N=16 rows x K=128] (K-major, 128B swizzle): row 0 all ones.
@@ -299,6 +294,7 @@ __global__ void __launch_bounds__(192, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(d_empty + 2);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
+    // 128 generator threads read each K stage (+ the MMA commit for V)
     for (int i = 0; i < kUpdStages; ++i) { mbar_init(kv_full + i, 1); mbar_init(kv_empty + i, 129); }
     for (int i = 0; i < kUpdPhiBufs; ++i) { mbar_init(phi_full + i, 128); mbar_init(phi_empty + i, 1); }
     for (int i = 0; i < 2; ++i) { mbar_init(d_full + i, 1); mbar_init(d_empty + i, 128); }
@@ -364,15 +360,15 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
     for (int n = 0; n < 65; ++n) state[n] = 0.f;
     bool ok = true;
-    // snapshots of chunks before the first delta that matters are all zero except chunk 0 (never used)
     for (int u = 0; u < n_sub && ok; ++u) {
       const int st = u % kUpdStages, pb = u % kUpdPhiBufs;
       if (!mbar_wait(kv_full + st, (u / kUpdStages) & 1, p.err, kErrPolyWait)) { ok = false; break; }
       if (!mbar_wait(phi_empty + pb, ((u / kUpdPhiBufs) & 1) ^ 1, p.err, kErrPolyWait)) { ok = false; break; }
-      float x[64];
-      load_row64(sKV + st * 32768, gt, x);
+      uint32_t hrow[32];
+      load_row_h2(sKV + st * 32768, gt, hrow);
       const float2 xi = fb < 32 ? load_pair(sKV + st * 32768, gt, 2 * fb) : make_float2(0.f, 0.f);
-      store_feature_block(sPhi + pb * 32768, gt, fb, x, xi, p.scale, rs, 1.0f);
+      store_feature_atom(sPhi + pb * 32768, gt, fb, 0, hrow, xi, p.scale, rs, 1.0f);
+      store_feature_atom(sPhi + pb * 32768, gt, fb, 1, hrow, xi, p.scale, rs, 1.0f);
       fence_async_smem();
       mbar_arrive(phi_full + pb);
       mbar_arrive(kv_empty + st);  // K rows read (the MMA commit covers V)
@@ -538,13 +534,14 @@ __global__ void __launch_bounds__(192, 1)
     PolyCtl ctl = *p.ctl;
     const float rs = sqrtf(p.scale);
     bool ok = mbar_wait(q_full, 0, p.err, kErrPolyWait);
-    float x[64];
-    if (ok) load_row64(sQ, r, x);
+    uint32_t hrow[32];
+    if (ok) load_row_h2(sQ, r, hrow);
     for (int kb = 0; kb < kPolyFeatBlocks && ok; ++kb) {
       const int pb = kb % kAppPhiBufs;
       if (!mbar_wait(phi_empty + pb, ((kb / kAppPhiBufs) & 1) ^ 1, p.err, kErrPolyWait)) { ok = false; break; }
       const float2 xi = kb < 32 ? load_pair(sQ, r, 2 * kb) : make_float2(0.f, 0.f);
-      store_feature_block(sPhi + pb * 32768, r, kb, x, xi, ctl.c2 * p.scale, ctl.c1 * rs, ctl.c0);
+      store_feature_atom(sPhi + pb * 32768, r, kb, 0, hrow, xi, ctl.c2 * p.scale, ctl.c1 * rs, ctl.c0);
+      store_feature_atom(sPhi + pb * 32768, r, kb, 1, hrow, xi, ctl.c2 * p.scale, ctl.c1 * rs, ctl.c0);
       fence_async_smem();
       mbar_arrive(phi_full + pb);
     }
