@@ -196,6 +196,13 @@ TJ_DEV void store_atom_row_h2(uint8_t* atom, int row, float coef, const uint32_t
     *reinterpret_cast<uint4*>(base + ((c ^ (row & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
   }
 }
+// w = coef * h (64 fp16 values as 32 pairs), packed fp16 multiplies.
+TJ_DEV void scale_row_h2(const uint32_t (&h)[32], float coef, uint32_t (&w)[32]) {
+  const __half2 c2 = __float2half2_rn(coef);
+  const uint32_t cw = *reinterpret_cast<const uint32_t*>(&c2);
+#pragma unroll
+  for (int e = 0; e < 32; ++e) asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(w[e]) : "r"(h[e]), "r"(cw));
+}
 // One atom row holding a single constant in feature 0 (the phi0 slot), zeros elsewhere.
 TJ_DEV void store_const_row(uint8_t* atom, int row, float c0) {
   uint8_t* base = atom + row * 128;
@@ -388,11 +395,11 @@ __global__ void __launch_bounds__(192, 1)
 }
 
 // ------------------------------------------------------------------ apply
-constexpr int kAppSnapStages = 3;  // snapshot K-block ring (2 x [80 x 64] fp16 = 20 KB)
+constexpr int kAppSnapStages = 6;  // snapshot K-block ring (2 x [80 x 64] fp16 = 20 KB)
 constexpr int kAppSnapBytes = 20480;
-constexpr int kAppPhiBufs = 2;
+constexpr int kAppPhiBufs = 2;     // phi_q feature blocks, in TMEM
 constexpr int kAppSmem = 16384 /*Q*/ + 2 * 32768 /*diag K,V ring*/ + kAppSnapStages * kAppSnapBytes +
-                         kAppPhiBufs * 32768 + 4096 /*ones*/ + 1024 + 256;
+                         4096 /*ones*/ + 1024 + 256;
 
 __global__ void __launch_bounds__(192, 1)
     poly_apply_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -411,8 +418,7 @@ __global__ void __launch_bounds__(192, 1)
   uint8_t* sQ = smem;
   uint8_t* sKV = sQ + 16384;                              // [2][K 16 KB | V 16 KB] -> 2 x 32 KB
   uint8_t* sSnap = sKV + 2 * 32768;
-  uint8_t* sPhi = sSnap + kAppSnapStages * kAppSnapBytes;
-  uint8_t* sOnes = sPhi + kAppPhiBufs * 32768;
+  uint8_t* sOnes = sSnap + kAppSnapStages * kAppSnapBytes;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sOnes + 4096);
   uint64_t* q_full = bars;
   uint64_t* sn_full = q_full + 1;
@@ -445,8 +451,8 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  // TMEM: inter acc [0, 80) | diag acc [128, 208) | S [256, 384) | P [384, 448)
-  const uint32_t t_inter = tmem, t_diag = tmem + 128, t_s = tmem + 256, t_p = tmem + 384;
+  // TMEM: inter acc [0, 80) | diag acc [80, 160) | phi_q [160, 224) [224, 288) | S [288, 416) | P [416, 480)
+  const uint32_t t_inter = tmem, t_diag = tmem + 80, t_phi = tmem + 160, t_s = tmem + 288, t_p = tmem + 416;
   const int row0 = bh * p.S;
   const int snap_row0 = (bh * (n_chunks - p.prefix_chunks) + (c - p.prefix_chunks)) * kPolyN;
 
@@ -478,19 +484,19 @@ __global__ void __launch_bounds__(192, 1)
       constexpr uint32_t idesc_p1 = idesc_f16_f32(128, 16, false, false);
       const uint32_t ones = smem_u32(sOnes);
       bool ok = true;
-      // phase 1: inter = phi_q(q) @ S_c over 33 feature blocks
+      // phase 1: inter = phi_q(q) @ S_c over 33 feature blocks; phi_q is the
+      // TMEM A operand (TS form), so only the snapshot passes through smem
       for (int kb = 0; kb < kPolyFeatBlocks && ok; ++kb) {
         const int st = kb % kAppSnapStages, pb = kb % kAppPhiBufs;
         if (!mbar_wait(sn_full + st, (kb / kAppSnapStages) & 1, p.err, kErrPolyWait)) { ok = false; break; }
         if (!mbar_wait(phi_full + pb, (kb / kAppPhiBufs) & 1, p.err, kErrPolyWait)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t phi = smem_u32(sPhi + pb * 32768);
+        const uint32_t phi = t_phi + pb * 64;
         const uint32_t sn = smem_u32(sSnap + st * kAppSnapBytes);
 #pragma unroll
-        for (int ks = 0; ks < 8; ++ks) {  // K = 128 features
-          const uint64_t ad = smem_desc(phi + (ks >> 2) * 16384 + (ks & 3) * 32, 16, 1024, 128);
+        for (int ks = 0; ks < 8; ++ks) {  // K = 128 features, 16 per MMA (8 TMEM columns)
           const uint64_t bd = smem_desc(sn + (ks >> 2) * 10240 + (ks & 3) * 32, 16, 1024, 128);
-          umma_f16_ss(t_inter, ad, bd, idesc_inter, (kb | ks) != 0);
+          umma_f16_ts(t_inter, phi + ks * 8, bd, idesc_inter, (kb | ks) != 0);
         }
         umma_commit(sn_empty + st);
         umma_commit(phi_empty + pb);
@@ -539,10 +545,24 @@ __global__ void __launch_bounds__(192, 1)
     for (int kb = 0; kb < kPolyFeatBlocks && ok; ++kb) {
       const int pb = kb % kAppPhiBufs;
       if (!mbar_wait(phi_empty + pb, ((kb / kAppPhiBufs) & 1) ^ 1, p.err, kErrPolyWait)) { ok = false; break; }
+      tc_fence_after();
       const float2 xi = kb < 32 ? load_pair(sQ, r, 2 * kb) : make_float2(0.f, 0.f);
-      store_feature_atom(sPhi + pb * 32768, r, kb, 0, hrow, xi, ctl.c2 * p.scale, ctl.c1 * rs, ctl.c0);
-      store_feature_atom(sPhi + pb * 32768, r, kb, 1, hrow, xi, ctl.c2 * p.scale, ctl.c1 * rs, ctl.c0);
-      fence_async_smem();
+      // this query row's 128 features as 64 fp16 pairs -> its TMEM lane
+      uint32_t w[32];
+      const float c_a = kb < 32 ? ctl.c2 * p.scale * xi.x : ctl.c1 * rs;
+      scale_row_h2(hrow, c_a, w);
+      tmem_st32(t_phi + pb * 64 + lane_off, w);
+      if (kb < 32) {
+        scale_row_h2(hrow, ctl.c2 * p.scale * xi.y, w);
+      } else {
+        const __half2 c0p = __floats2half2_rn(ctl.c0, 0.f);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) w[i] = 0u;
+        w[0] = *reinterpret_cast<const uint32_t*>(&c0p);
+      }
+      tmem_st32(t_phi + pb * 64 + lane_off + 32, w);
+      tmem_st_wait();
+      tc_fence_before();
       mbar_arrive(phi_full + pb);
     }
     const int qpos = (sblk * 128) + r;  // query position inside the chunk
