@@ -324,6 +324,7 @@ struct Workspace {
   __half* ff;   // [M, F]
   tj::PolyCtl* poly_ctl;  // polynomial route (null when the route cannot run)
   __half* poly_snap;
+  __half* poly_kt;        // K transposed [B, H, 64, S] for the polynomial update
 };
 
 // Exact prefix of the polynomial route (the reference's EXACT_PREFIX) and the
@@ -365,9 +366,11 @@ size_t carve(const TjConfig& c, int B, int S, int route, uint8_t* base, Workspac
   t.ff = reinterpret_cast<__half*>(take(2 * M * c.ffn_dim));
   t.poly_ctl = nullptr;
   t.poly_snap = nullptr;
+  t.poly_kt = nullptr;
   if (poly_eligible(c, S, route)) {
     t.poly_ctl = reinterpret_cast<tj::PolyCtl*>(take(sizeof(tj::PolyCtl)));
     t.poly_snap = reinterpret_cast<__half*>(take(2 * poly_snap_elems(B * c.num_heads, S)));
+    t.poly_kt = reinterpret_cast<__half*>(take(2 * (size_t)B * c.num_heads * 64 * S));
   }
   if (w) *w = t;
   return off;
@@ -429,11 +432,23 @@ int timed_launch(TjModel* m, int cls, int kernels, cudaStream_t st, F&& launch) 
 // Polynomial route for one layer: guard -> (exact prefix | whole sequence if
 // not admitted) on the flash kernel -> state update -> apply.  All admission
 // decisions stay on the device.
+// K^T and the update kernel (shared by the single-GPU and the sequence-sharded routes).
+int launch_poly_update(const tj::PolyParams& pp, const CUtensorMap& tv, cudaStream_t st) {
+  const int BH = pp.B * pp.H;
+  tj::poly_k_transpose_kernel<<<dim3(pp.S / 64, BH), 256, 0, st>>>(pp.k, pp.kt, pp.S);
+  TJ_CUDA(cudaGetLastError());
+  CUtensorMap tkt;
+  TJ_CHECK(make_map_f16(&tkt, pp.kt, (uint64_t)BH * 64, (uint64_t)pp.S, 64, 64, 128));
+  tj::poly_update_kernel<<<dim3(tj::kPolyFeatBlocks, BH), 192, tj::kUpdSmem, st>>>(tkt, tv, pp);
+  TJ_CUDA(cudaGetLastError());
+  return TJ_OK;
+}
+
 int launch_poly_route(const __half* q, const __half* k, const __half* v, __half* ctx, const int* lengths, int B,
-                      int H, int S, int d_model, int exact_prefix, tj::PolyCtl* ctl, __half* snap, TjModel* m,
-                      const tj::AttnParams& ap_in, cudaStream_t st) {
+                      int H, int S, int d_model, int exact_prefix, tj::PolyCtl* ctl, __half* snap, __half* kt,
+                      TjModel* m, const tj::AttnParams& ap_in, cudaStream_t st) {
   tj::PolyParams pp{};
-  pp.q = q; pp.k = k; pp.v = v; pp.ctx = ctx; pp.snap = snap; pp.ctl = ctl; pp.lengths = lengths;
+  pp.q = q; pp.k = k; pp.v = v; pp.ctx = ctx; pp.snap = snap; pp.kt = kt; pp.ctl = ctl; pp.lengths = lengths;
   pp.B = B; pp.H = H; pp.S = S; pp.d_model = d_model;
   pp.prefix_chunks = exact_prefix / tj::kPolyChunk;
   pp.scale = 0.125f;  // 64^-0.5
@@ -473,11 +488,7 @@ int launch_poly_route(const __half* q, const __half* k, const __half* v, __half*
     TJ_CUDA(cudaFuncSetAttribute(tj::poly_apply_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, tj::kAppSmem));
     attr_set[dev] = true;
   }
-  TJ_CHECK(timed_launch(m, TJ_K_POLY, 1, st, [&]() -> int {
-    tj::poly_update_kernel<<<dim3(tj::kPolyFeatBlocks, B * H), 192, tj::kUpdSmem, st>>>(tk, tv, pp);
-    TJ_CUDA(cudaGetLastError());
-    return TJ_OK;
-  }));
+  TJ_CHECK(timed_launch(m, TJ_K_POLY, 2, st, [&]() -> int { return launch_poly_update(pp, tv, st); }));
   TJ_CHECK(timed_launch(m, TJ_K_POLY, 1, st, [&]() -> int {
     tj::poly_apply_kernel<<<dim3((n_chunks - pp.prefix_chunks) * 4, B * H), 192, tj::kAppSmem, st>>>(tq, tk, tv, tsn,
                                                                                                    pp);
@@ -681,7 +692,7 @@ int tj_forward(TjModel* m, const float* x, const uint8_t* mask, float* out, int 
     // route (device-side guard; the flash kernel then covers the exact prefix)
     if (w.poly_ctl != nullptr) {
       TJ_CHECK(launch_poly_route(w.q, w.k, w.v, w.act, w.lengths, B, H, S, d, kPolyExactPrefix, w.poly_ctl,
-                                 w.poly_snap, m, ap, st));
+                                 w.poly_snap, w.poly_kt, m, ap, st));
     } else {
       TJ_CHECK(timed_launch(m, TJ_K_ATTN, 1, st, [&] { return launch_attention(w.q, w.k, w.v, hd, ap, B, st); }));
     }
@@ -764,7 +775,8 @@ int tj_poly_workspace_bytes(int B, int H, int S, int exact_prefix, size_t* bytes
   if (S % tj::kPolyChunk || exact_prefix % tj::kPolyChunk || exact_prefix < tj::kPolyChunk || exact_prefix >= S)
     return fail(TJ_ERR_UNSUPPORTED, "polynomial route needs seq_len and exact_prefix multiples of 512, 512 <= prefix < seq_len");
   const size_t n_snap = (size_t)(S - exact_prefix) / tj::kPolyChunk;
-  *bytes = align_up(sizeof(tj::PolyCtl), 256) + 2 * (size_t)B * H * n_snap * tj::kPolyN * tj::kPolyFeat;
+  *bytes = align_up(sizeof(tj::PolyCtl), 256) + 2 * (size_t)B * H * n_snap * tj::kPolyN * tj::kPolyFeat +
+           2 * (size_t)B * H * 64 * S;  // snapshots, then K^T
   return TJ_OK;
 }
 
@@ -779,6 +791,7 @@ int tj_poly_attention_f16(const void* q, const void* k, const void* v, void* ctx
   TJ_CHECK(device_info(&di));
   auto* ctl = static_cast<tj::PolyCtl*>(ws);
   auto* snap = reinterpret_cast<__half*>(static_cast<uint8_t*>(ws) + align_up(sizeof(tj::PolyCtl), 256));
+  __half* kt = snap + (size_t)B * H * ((S - exact_prefix) / tj::kPolyChunk) * tj::kPolyN * tj::kPolyFeat;
   tj::AttnParams ap{};
   ap.lengths = lengths; ap.mask = nullptr; ap.general = nullptr; ap.ctx = static_cast<__half*>(ctx);
   ap.S = S; ap.H = H; ap.d_model = H * 64; ap.causal = 1;
@@ -790,7 +803,7 @@ int tj_poly_attention_f16(const void* q, const void* k, const void* v, void* ctx
   ap.B = B;
   return launch_poly_route(static_cast<const __half*>(q), static_cast<const __half*>(k),
                            static_cast<const __half*>(v), static_cast<__half*>(ctx), lengths, B, H, S, H * 64,
-                           exact_prefix, ctl, snap, nullptr, ap, static_cast<cudaStream_t>(stream));
+                           exact_prefix, ctl, snap, kt, nullptr, ap, static_cast<cudaStream_t>(stream));
 }
 
 int tj_profile_begin(TjModel* m, int max_launches) {
@@ -915,6 +928,7 @@ struct ShardWorkspace {
   Workspace base;
   tj::PolyCtl* ctl;
   __half* snap;
+  __half* kt;       // [B][H][64][S_loc]: this shard's K transposed
   float* total;     // [B*H][80][4224] fp32: this shard's state
   float* gathered;  // [world][B*H][80][4224]
   __half* kg;       // [world][B][H][S_loc][64]: every shard's K (exact route)
@@ -942,6 +956,7 @@ size_t carve_shard(const TjConfig& c, int B, int S_loc, int world, int route, ui
     const size_t state = BH * tj::kPolyN * tj::kPolyFeat;
     t.ctl = reinterpret_cast<tj::PolyCtl*>(take(sizeof(tj::PolyCtl)));
     t.snap = reinterpret_cast<__half*>(take(2 * BH * (S_loc / tj::kPolyChunk) * tj::kPolyN * tj::kPolyFeat));
+    t.kt = reinterpret_cast<__half*>(take(2 * BH * 64 * (size_t)S_loc));
     t.total = reinterpret_cast<float*>(take(4 * state));
     t.gathered = reinterpret_cast<float*>(take(4 * state * world));
   }
@@ -969,7 +984,8 @@ int shard_attention(TjModel* m, TjComm* cm, ShardWorkspace& w, int B, int S_loc,
   bool admit = false;
   if (w.ctl != nullptr) {
     tj::PolyParams pp{};
-    pp.q = w.base.q; pp.k = w.base.k; pp.v = w.base.v; pp.ctx = w.base.act; pp.snap = w.snap; pp.ctl = w.ctl;
+    pp.q = w.base.q; pp.k = w.base.k; pp.v = w.base.v; pp.ctx = w.base.act; pp.snap = w.snap; pp.kt = w.kt;
+    pp.ctl = w.ctl;
     pp.lengths = w.base.lengths;
     pp.B = B; pp.H = H; pp.S = S_loc; pp.d_model = d;
     pp.prefix_chunks = rank == 0 ? kPolyExactPrefix / tj::kPolyChunk : 0;
@@ -1004,11 +1020,7 @@ int shard_attention(TjModel* m, TjComm* cm, ShardWorkspace& w, int B, int S_loc,
       TJ_CHECK(make_map_f16(&tsn, w.snap, snap_rows, tj::kPolyFeat, tj::kPolyN, 64, 128));
       TJ_CUDA(cudaFuncSetAttribute(tj::poly_update_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, tj::kUpdSmem));
       TJ_CUDA(cudaFuncSetAttribute(tj::poly_apply_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, tj::kAppSmem));
-      TJ_CHECK(timed_launch(m, TJ_K_POLY, 1, st, [&]() -> int {
-        tj::poly_update_kernel<<<dim3(tj::kPolyFeatBlocks, B * H), 192, tj::kUpdSmem, st>>>(tk, tv, pp);
-        TJ_CUDA(cudaGetLastError());
-        return TJ_OK;
-      }));
+      TJ_CHECK(timed_launch(m, TJ_K_POLY, 2, st, [&]() -> int { return launch_poly_update(pp, tv, st); }));
       const size_t state = (size_t)B * H * tj::kPolyN * tj::kPolyFeat;
       TJ_CHECK(nccl_check(cm, nc.AllGather(w.total, w.gathered, state, ncclFloat32, cm->comm, st), "state all-gather"));
       if (rank > 0) {

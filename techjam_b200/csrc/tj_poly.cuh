@@ -21,15 +21,18 @@
 //       Hermite coefficients), on the device: no host synchronisation.  Every
 //       poly kernel exits at once unless admitted; the flash kernel then covers
 //       the whole sequence instead of only the exact prefix.
+//   poly_k_transpose_kernel  K^T per head, so feature rows are contiguous.
 //   poly_update_kernel  one CTA per (128-feature block, head): per 128-token
-//       sub-chunk it builds phi_k on the CUDA cores into shared memory and
-//       accumulates phi_k^T [v | 1] in TMEM (double-buffered per chunk); the
+//       sub-chunk each thread forms one feature row (over the tokens) and
+//       stores it to its TMEM lane, the tensor core accumulates
+//       phi_k^T [v | 1] (A from TMEM) in TMEM (double-buffered per chunk); the
 //       running state stays in registers (fp32) and after every chunk the
 //       MEAN state S_c / (512 c) is stored as fp16 (keeps the fp16 snapshot in
 //       range however long the sequence).
 //   poly_apply_kernel   one CTA per (128-query block, head): phi_q(q) @ S_c
-//       over 33 feature blocks (K = 4224) plus the exact-exp diagonal block,
-//       then out = (512c * inter + diag)[:64] / (512c * inter + diag)[64].
+//       over 33 feature blocks (K = 4224; phi_q rows written to TMEM as the A
+//       operand) plus the exact-exp diagonal block, then
+//       out = (512c * inter + diag)[:64] / (512c * inter + diag)[64].
 #pragma once
 #include "tj_common.cuh"
 
@@ -56,6 +59,7 @@ struct PolyParams {
   const __half* k;
   const __half* v;
   __half* ctx;      // [B*S, d_model]
+  __half* kt;       // [B, H, 64, S] fp16: K transposed (the update kernel's feature rows)
   __half* snap;     // [B*H][n_snap][80][4224] fp16 mean states
   PolyCtl* ctl;
   const int* lengths;
@@ -158,12 +162,10 @@ __global__ void poly_guard_finalize(PolyParams p) {
   c->admit = ok ? 1 : 0;
 }
 
-// ------------------------------------------------------------------ feature tiles
-// A feature tile is [128 token rows x 128 features] fp16 stored as two
-// 64-feature atoms of [128 rows x 128 B] with the 128-byte swizzle (16-byte
-// chunk c of row r at c ^ (r & 7)).  The same bytes serve as the K-major A
-// operand of the apply GEMM (M = tokens, K = features) and as the MN-major A
-// operand of the update GEMM (M = features, K = tokens).
+// ------------------------------------------------------------------ feature rows
+// Q, K, V tiles are [128 rows x 64] fp16 with the 128-byte swizzle (16-byte
+// chunk c of row r at c ^ (r & 7)); feature maps are formed in registers and
+// written to TMEM, where they are the A operand of the tensor-core products.
 // Row `row` of a [128 x 64] fp16 tile (128-byte swizzle) as 32 packed halves pairs.
 TJ_DEV void load_row_h2(const uint8_t* tile, int row, uint32_t (&h)[32]) {
   const uint8_t* base = tile + row * 128;
@@ -180,22 +182,6 @@ TJ_DEV float2 load_pair(const uint8_t* tile, int row, int i) {
   return __half22float2(*reinterpret_cast<const __half2*>(a));
 }
 
-// One atom row: feature j = coef * x[j] (j = 0..63), as packed fp16
-// multiplies (coef rounded to fp16 once; for the key side's quadratic block
-// coef = k_i / 8 is exact, so those features are the correctly rounded
-// products).
-TJ_DEV void store_atom_row_h2(uint8_t* atom, int row, float coef, const uint32_t (&h)[32]) {
-  const __half2 c2 = __float2half2_rn(coef);
-  const uint32_t cw = *reinterpret_cast<const uint32_t*>(&c2);
-  uint8_t* base = atom + row * 128;
-#pragma unroll
-  for (int c = 0; c < 8; ++c) {
-    uint32_t w[4];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(w[e]) : "r"(h[4 * c + e]), "r"(cw));
-    *reinterpret_cast<uint4*>(base + ((c ^ (row & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
-  }
-}
 // w = coef * h (64 fp16 values as 32 pairs), packed fp16 multiplies.
 TJ_DEV void scale_row_h2(const uint32_t (&h)[32], float coef, uint32_t (&w)[32]) {
   const __half2 c2 = __float2half2_rn(coef);
@@ -203,29 +189,6 @@ TJ_DEV void scale_row_h2(const uint32_t (&h)[32], float coef, uint32_t (&w)[32])
 #pragma unroll
   for (int e = 0; e < 32; ++e) asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(w[e]) : "r"(h[e]), "r"(cw));
 }
-// One atom row holding a single constant in feature 0 (the phi0 slot), zeros elsewhere.
-TJ_DEV void store_const_row(uint8_t* atom, int row, float c0) {
-  uint8_t* base = atom + row * 128;
-#pragma unroll
-  for (int c = 0; c < 8; ++c) {
-    uint4 w = make_uint4(0u, 0u, 0u, 0u);
-    if (c == 0) w.x = pack_half2(c0, 0.f);
-    *reinterpret_cast<uint4*>(base + ((c ^ (row & 7)) << 4)) = w;
-  }
-}
-
-// Writes atom `a` (0: first, 1: second 64 features) of feature block fb of
-// this token row (h = the row, xi = its elements 2fb and 2fb+1).  quad/lin/cst
-// are the phi2, phi1 and phi0 coefficients (key side: scale, sqrt(scale), 1;
-// query side folded with c2, c1, c0).
-TJ_DEV void store_feature_atom(uint8_t* tile, int row, int fb, int a, const uint32_t (&h)[32], float2 xi,
-                               float quad, float lin, float cst) {
-  uint8_t* atom = tile + a * 16384;
-  if (fb < 32) store_atom_row_h2(atom, row, quad * (a == 0 ? xi.x : xi.y), h);
-  else if (a == 0) store_atom_row_h2(atom, row, lin, h);
-  else store_const_row(atom, row, cst);
-}
-
 // The constant B operand [N=16 rows x K=128] (K-major, 128B swizzle): row 0 all ones.
 TJ_DEV void init_ones_tile(uint8_t* ones, int tid, int nthreads) {
   for (int i = tid; i < 4096 / 16; i += nthreads) {  // 2 atoms x 16 rows x 8 chunks
@@ -235,10 +198,11 @@ TJ_DEV void init_ones_tile(uint8_t* ones, int tid, int nthreads) {
   }
 }
 
-// Chunk c's delta (TMEM buffer c & 1) -> running fp32 state (registers) ->
-// fp16 MEAN snapshot for chunk c+1 (row frow of feature block fb).
+// Chunk c's delta (TMEM buffer c & 1), times the feature row's coefficient
+// (scale, sqrt(scale) or 1), -> running fp32 state (registers) -> fp16 MEAN
+// snapshot for chunk c+1 (row frow of feature block fb).
 TJ_DEV bool update_drain(const PolyParams& p, uint32_t tmem, int quarter, int frow, int fb, int bh, int c,
-                         int n_chunks, uint64_t* d_full, uint64_t* d_empty, float (&state)[65]) {
+                         int n_chunks, uint64_t* d_full, uint64_t* d_empty, float coef, float (&state)[65]) {
   const int db = c & 1;
   if (!mbar_wait(d_full + db, (c >> 1) & 1, p.err, kErrPolyWait)) return false;
   tc_fence_after();
@@ -250,7 +214,7 @@ TJ_DEV bool update_drain(const PolyParams& p, uint32_t tmem, int quarter, int fr
     tmem_ld_wait();
 #pragma unroll
     for (int i = 0; i < 32; ++i)
-      if (part * 32 + i < 65) state[part * 32 + i] += __uint_as_float(r[i]);
+      if (part * 32 + i < 65) state[part * 32 + i] = fmaf(coef, __uint_as_float(r[i]), state[part * 32 + i]);
   }
   tc_fence_before();
   mbar_arrive(d_empty + db);
@@ -272,12 +236,53 @@ TJ_DEV bool update_drain(const PolyParams& p, uint32_t tmem, int quarter, int fr
 }
 
 // ------------------------------------------------------------------ update
-constexpr int kUpdStages = 4;     // K/V sub-chunk ring
-constexpr int kUpdPhiBufs = 2;
-constexpr int kUpdSmem = kUpdStages * 32768 + kUpdPhiBufs * 32768 + 4096 + 1024 + 256;
+// kt[bh][d][t] = k[bh][t][d]: the update kernel reads feature rows (a key
+// dimension over 128 tokens) as contiguous shared-memory rows.
+__global__ void __launch_bounds__(256) poly_k_transpose_kernel(const __half* __restrict__ k, __half* __restrict__ kt,
+                                                               int S) {
+  __shared__ __half tile[64][72];  // [token][dim], 16-byte padded rows
+  const int bh = blockIdx.y;
+  const int t0 = blockIdx.x * 64;
+  const __half* src = k + ((size_t)bh * S + t0) * 64;
+  for (int i = threadIdx.x; i < 512; i += blockDim.x) {
+    const int r = i >> 3, c = (i & 7) * 8;
+    *reinterpret_cast<uint4*>(&tile[r][c]) = *reinterpret_cast<const uint4*>(src + (size_t)r * 64 + c);
+  }
+  __syncthreads();
+  __half* dst = kt + (size_t)bh * 64 * S + t0;
+  for (int i = threadIdx.x; i < 512; i += blockDim.x) {
+    const int d = i >> 3, c = (i & 7) * 8;
+    __align__(16) __half v[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = tile[c + e][d];
+    *reinterpret_cast<uint4*>(dst + (size_t)d * S + c) = *reinterpret_cast<const uint4*>(v);
+  }
+}
 
+// 64 halves (32 pairs) of row `row` of a [64 x 64] fp16 box with the 128-byte swizzle.
+TJ_DEV void load_box_row(const uint8_t* box, int row, uint32_t* h) {
+  const uint8_t* base = box + row * 128;
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    const uint4 w = *reinterpret_cast<const uint4*>(base + ((c ^ (row & 7)) << 4));
+    h[4 * c] = w.x; h[4 * c + 1] = w.y; h[4 * c + 2] = w.z; h[4 * c + 3] = w.w;
+  }
+}
+
+constexpr int kUpdStages = 5;     // K^T / V sub-chunk ring
+constexpr int kUpdPhiBufs = 2;    // phi_k sub-chunk tiles, in TMEM
+constexpr int kUpdSmem = kUpdStages * 32768 + 4096 + 1024 + 256;
+
+// One CTA per (128-feature block fb, head).  Thread L of the generator warps
+// owns feature row L of the block (TMEM lane L): for fb < 32 the product
+// k_{2fb + L/64} * k_{L%64} over the sub-chunk's 128 tokens (packed fp16
+// multiplies of two K^T rows), for fb = 32 the linear rows k_L (L < 64), the
+// constant row (L = 64) and zeros; its coefficient (scale, sqrt(scale), 1) is
+// applied when the chunk's delta is drained.  The rows go straight into TMEM
+// as the A operand of phi_k^T [V | 1] (TS form), so shared memory carries only
+// K^T and V.
 __global__ void __launch_bounds__(192, 1)
-    poly_update_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+    poly_update_kernel(const __grid_constant__ CUtensorMap tmKt, const __grid_constant__ CUtensorMap tmV,
                        const PolyParams p) {
   if (p.ctl->admit == 0 || error_raised(p.err)) return;
   const int fb = blockIdx.x;
@@ -288,9 +293,8 @@ __global__ void __launch_bounds__(192, 1)
   if (n_sub <= 0) return;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sKV = smem;                                  // stage: K 16 KB | V 16 KB
-  uint8_t* sPhi = sKV + kUpdStages * 32768;             // [2][32 KB]
-  uint8_t* sOnes = sPhi + kUpdPhiBufs * 32768;          // 4 KB
+  uint8_t* sKV = smem;                                  // stage: K^T 2 x 8 KB | V 16 KB
+  uint8_t* sOnes = sKV + kUpdStages * 32768;            // 4 KB
   uint64_t* bars = reinterpret_cast<uint64_t*>(sOnes + 4096);
   uint64_t* kv_full = bars;
   uint64_t* kv_empty = kv_full + kUpdStages;
@@ -301,37 +305,40 @@ __global__ void __launch_bounds__(192, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(d_empty + 2);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    // 128 generator threads read each K stage (+ the MMA commit for V)
+    // 128 generator threads read each K^T stage (+ the MMA commit for V)
     for (int i = 0; i < kUpdStages; ++i) { mbar_init(kv_full + i, 1); mbar_init(kv_empty + i, 129); }
     for (int i = 0; i < kUpdPhiBufs; ++i) { mbar_init(phi_full + i, 128); mbar_init(phi_empty + i, 1); }
     for (int i = 0; i < 2; ++i) { mbar_init(d_full + i, 1); mbar_init(d_empty + i, 128); }
     fence_mbar_init();
   }
   if (warp >= 2) init_ones_tile(sOnes, threadIdx.x - 64, 128);
-  if (warp == 1) { tmem_alloc(tmem_slot, 256); tmem_relinquish(); }
+  if (warp == 1) { tmem_alloc(tmem_slot, 512); tmem_relinquish(); }
   fence_async_smem();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // TMEM: deltas [0, 128) [128, 256) (N = 64 + 16 each) | phi_k [256, 320) [320, 384)
+  const uint32_t t_phi = tmem + 256;
   const int row0 = bh * p.S;
 
   if (warp == 0) {
     if (lane == 0) {
-      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmKt);
       tma_prefetch_desc(&tmV);
       for (int u = 0; u < n_sub; ++u) {
         const int st = u % kUpdStages;
         if (!mbar_wait(kv_empty + st, ((u / kUpdStages) & 1) ^ 1, p.err, kErrPolyWait)) break;
         mbar_expect_tx(kv_full + st, 32768);
-        tma_load_2d(sKV + st * 32768, &tmK, kv_full + st, 0, row0 + u * 128);
+        tma_load_2d(sKV + st * 32768, &tmKt, kv_full + st, u * 128, bh * 64);
+        tma_load_2d(sKV + st * 32768 + 8192, &tmKt, kv_full + st, u * 128 + 64, bh * 64);
         tma_load_2d(sKV + st * 32768 + 16384, &tmV, kv_full + st, 0, row0 + u * 128);
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idesc_v = idesc_f16_f32(128, 64, true, true);     // A MN-major, B MN-major
-      constexpr uint32_t idesc_1 = idesc_f16_f32(128, 16, true, false);    // A MN-major, B K-major
+      constexpr uint32_t idesc_v = idesc_f16_f32(128, 64, false, true);   // A from TMEM, B (V) MN-major
+      constexpr uint32_t idesc_1 = idesc_f16_f32(128, 16, false, false);  // B (ones) K-major
       const uint32_t ones = smem_u32(sOnes);
       bool ok = true;
       for (int u = 0; u < n_sub && ok; ++u) {
@@ -341,16 +348,15 @@ __global__ void __launch_bounds__(192, 1)
         if (!mbar_wait(kv_full + st, (u / kUpdStages) & 1, p.err, kErrPolyWait)) { ok = false; break; }
         if (!mbar_wait(phi_full + pb, (u / kUpdPhiBufs) & 1, p.err, kErrPolyWait)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t phi = smem_u32(sPhi + pb * 32768);
+        const uint32_t phi = t_phi + pb * 64;
         const uint32_t vv = smem_u32(sKV + st * 32768 + 16384);
         const uint32_t d = tmem + db * 128;
 #pragma unroll
-        for (int ks = 0; ks < 8; ++ks) {  // K = 128 tokens, 16 per MMA
-          const uint64_t ad = smem_desc(phi + ks * 2048, 16384, 1024, 128);
+        for (int ks = 0; ks < 8; ++ks) {  // K = 128 tokens, 16 per MMA (8 TMEM columns)
           const uint64_t bv = smem_desc(vv + ks * 2048, 8192, 1024, 128);
           const uint64_t b1 = smem_desc(ones + (ks >> 2) * 2048 + (ks & 3) * 32, 16, 1024, 128);
-          umma_f16_ss(d, ad, bv, idesc_v, ((u & 3) | ks) != 0);
-          umma_f16_ss(d + 64, ad, b1, idesc_1, ((u & 3) | ks) != 0);
+          umma_f16_ts(d, phi + ks * 8, bv, idesc_v, ((u & 3) | ks) != 0);
+          umma_f16_ts(d + 64, phi + ks * 8, b1, idesc_1, ((u & 3) | ks) != 0);
         }
         umma_commit(kv_empty + st);
         umma_commit(phi_empty + pb);
@@ -358,11 +364,12 @@ __global__ void __launch_bounds__(192, 1)
       }
     }
   } else {
-    // ---------------------------------------------------- phi_k producer + state epilogue
-    const int gt = threadIdx.x - 64;      // token row for generation
-    const int quarter = warp & 3;         // TMEM lanes of this warp (feature rows)
-    const int frow = quarter * 32 + lane; // feature row of this thread in the epilogue
-    const float rs = sqrtf(p.scale);
+    // ---------------------------------------------------- phi_k rows + state epilogue
+    const int quarter = warp & 3;          // TMEM lanes of this warp
+    const int frow = quarter * 32 + lane;  // feature row of this thread (generation and epilogue)
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const int a = frow >> 6, j = frow & 63;
+    const float coef = fb < 32 ? p.scale : (frow < 64 ? sqrtf(p.scale) : 1.0f);
     float state[65];
 #pragma unroll
     for (int n = 0; n < 65; ++n) state[n] = 0.f;
@@ -371,27 +378,43 @@ __global__ void __launch_bounds__(192, 1)
       const int st = u % kUpdStages, pb = u % kUpdPhiBufs;
       if (!mbar_wait(kv_full + st, (u / kUpdStages) & 1, p.err, kErrPolyWait)) { ok = false; break; }
       if (!mbar_wait(phi_empty + pb, ((u / kUpdPhiBufs) & 1) ^ 1, p.err, kErrPolyWait)) { ok = false; break; }
-      uint32_t hrow[32];
-      load_row_h2(sKV + st * 32768, gt, hrow);
-      const float2 xi = fb < 32 ? load_pair(sKV + st * 32768, gt, 2 * fb) : make_float2(0.f, 0.f);
-      store_feature_atom(sPhi + pb * 32768, gt, fb, 0, hrow, xi, p.scale, rs, 1.0f);
-      store_feature_atom(sPhi + pb * 32768, gt, fb, 1, hrow, xi, p.scale, rs, 1.0f);
-      fence_async_smem();
+      tc_fence_after();
+      const uint8_t* kt_st = sKV + st * 32768;
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {  // tokens 64*hh .. +63 -> TMEM columns 32*hh .. +31
+        uint32_t w[32];
+        if (fb < 32) {
+          uint32_t ki[32];
+          load_box_row(kt_st + hh * 8192, j, w);
+          load_box_row(kt_st + hh * 8192, 2 * fb + a, ki);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(w[e]) : "r"(w[e]), "r"(ki[e]));
+        } else if (frow < 64) {
+          load_box_row(kt_st + hh * 8192, j, w);
+        } else {
+          const uint32_t fill = frow == 64 ? 0x3C003C00u : 0u;  // the constant feature: 1 per token
+#pragma unroll
+          for (int e = 0; e < 32; ++e) w[e] = fill;
+        }
+        tmem_st32(t_phi + pb * 64 + hh * 32 + lane_off, w);
+      }
+      tmem_st_wait();
+      tc_fence_before();
       mbar_arrive(phi_full + pb);
-      mbar_arrive(kv_empty + st);  // K rows read (the MMA commit covers V)
+      mbar_arrive(kv_empty + st);  // K^T rows read (the MMA commit covers V)
       // drain the previous chunk's delta once this chunk's first sub-chunk is queued
       if ((u & 3) == 0 && u >= 4 &&
-          !update_drain(p, tmem, quarter, frow, fb, bh, (u >> 2) - 1, n_chunks, d_full, d_empty, state)) {
+          !update_drain(p, tmem, quarter, frow, fb, bh, (u >> 2) - 1, n_chunks, d_full, d_empty, coef, state)) {
         ok = false;
         break;
       }
     }
-    if (ok) update_drain(p, tmem, quarter, frow, fb, bh, (n_sub >> 2) - 1, n_chunks, d_full, d_empty, state);
+    if (ok) update_drain(p, tmem, quarter, frow, fb, bh, (n_sub >> 2) - 1, n_chunks, d_full, d_empty, coef, state);
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem, 256);
+  if (warp == 1) tmem_dealloc(tmem, 512);
 }
 
 // ------------------------------------------------------------------ apply
