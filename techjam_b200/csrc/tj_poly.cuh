@@ -12,9 +12,10 @@
 // phi_q(q) . phi_k(k) = w(q.k * scale), so for every query of chunk c
 //     [num | den] = phi_q(q) @ S_c + sum_{j in chunk, j <= i} exp(s_ij) [v_j | 1]
 // where S_c = sum over keys before chunk c of phi_k(k)^T [v | 1]  (4224 x 65).
-// A constant "ones" B tile makes the denominator column 64 of the same
-// accumulator, so numerator and denominator of all three polynomial orders
-// come out of one N=80 tensor-core accumulation.
+// The snapshots keep the denominator as column 64 of S_c, so in the apply
+// kernel numerator and denominator of all three polynomial orders come out of
+// one N = 80 tensor-core accumulation; the update kernel forms that column
+// and the exact diagonal block's denominator as per-thread FP32 row sums.
 //
 //   poly_guard_kernel/poly_guard_finalize  score std (sigma) and max |s| over a
 //       fixed strided sample of 512 rows per head -> PolyCtl (admit flag and
@@ -189,33 +190,27 @@ TJ_DEV void scale_row_h2(const uint32_t (&h)[32], float coef, uint32_t (&w)[32])
 #pragma unroll
   for (int e = 0; e < 32; ++e) asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(w[e]) : "r"(h[e]), "r"(cw));
 }
-// The constant B operand [N=16 rows x K=128] (K-major, 128B swizzle): row 0 all ones.
-TJ_DEV void init_ones_tile(uint8_t* ones, int tid, int nthreads) {
-  for (int i = tid; i < 4096 / 16; i += nthreads) {  // 2 atoms x 16 rows x 8 chunks
-    const int row = (i >> 3) & 15;
-    const uint32_t one2 = row == 0 ? 0x3C003C00u : 0u;  // two fp16 1.0
-    *reinterpret_cast<uint4*>(ones + i * 16) = make_uint4(one2, one2, one2, one2);
-  }
-}
 
-// Chunk c's delta (TMEM buffer c & 1), times the feature row's coefficient
-// (scale, sqrt(scale) or 1), -> running fp32 state (registers) -> fp16 MEAN
-// snapshot for chunk c+1 (row frow of feature block fb).
+// Chunk c's delta (numerator from TMEM buffer c & 1, denominator `den` summed
+// by the thread itself), times the feature row's coefficient (scale,
+// sqrt(scale) or 1), -> running fp32 state (registers) -> fp16 MEAN snapshot
+// for chunk c+1 (row frow of feature block fb).
 TJ_DEV bool update_drain(const PolyParams& p, uint32_t tmem, int quarter, int frow, int fb, int bh, int c,
-                         int n_chunks, uint64_t* d_full, uint64_t* d_empty, float coef, float (&state)[65]) {
+                         int n_chunks, uint64_t* d_full, uint64_t* d_empty, float coef, float den,
+                         float (&state)[65]) {
   const int db = c & 1;
   if (!mbar_wait(d_full + db, (c >> 1) & 1, p.err, kErrPolyWait)) return false;
   tc_fence_after();
   uint32_t r[32];
   const uint32_t a = tmem + ((uint32_t)(quarter * 32) << 16) + db * 128;
 #pragma unroll
-  for (int part = 0; part < 3; ++part) {
+  for (int part = 0; part < 2; ++part) {
     tmem_ld32(a + part * 32, r);
     tmem_ld_wait();
 #pragma unroll
-    for (int i = 0; i < 32; ++i)
-      if (part * 32 + i < 65) state[part * 32 + i] = fmaf(coef, __uint_as_float(r[i]), state[part * 32 + i]);
+    for (int i = 0; i < 32; ++i) state[part * 32 + i] = fmaf(coef, __uint_as_float(r[i]), state[part * 32 + i]);
   }
+  state[64] = fmaf(coef, den, state[64]);
   tc_fence_before();
   mbar_arrive(d_empty + db);
   const int cn = c + 1;
@@ -271,7 +266,7 @@ TJ_DEV void load_box_row(const uint8_t* box, int row, uint32_t* h) {
 
 constexpr int kUpdStages = 5;     // K^T / V sub-chunk ring
 constexpr int kUpdPhiBufs = 2;    // phi_k sub-chunk tiles, in TMEM
-constexpr int kUpdSmem = kUpdStages * 32768 + 4096 + 1024 + 256;
+constexpr int kUpdSmem = kUpdStages * 32768 + 1024 + 256;
 
 // One CTA per (128-feature block fb, head).  Thread L of the generator warps
 // owns feature row L of the block (TMEM lane L): for fb < 32 the product
@@ -279,8 +274,10 @@ constexpr int kUpdSmem = kUpdStages * 32768 + 4096 + 1024 + 256;
 // multiplies of two K^T rows), for fb = 32 the linear rows k_L (L < 64), the
 // constant row (L = 64) and zeros; its coefficient (scale, sqrt(scale), 1) is
 // applied when the chunk's delta is drained.  The rows go straight into TMEM
-// as the A operand of phi_k^T [V | 1] (TS form), so shared memory carries only
-// K^T and V.
+// as the A operand of phi_k^T V (TS form), so shared memory carries only K^T
+// and V; the denominator column phi_k^T 1 is each thread's own row sum (FP32
+// adds of the fp16 features), which saves the N = 16 MMA per 16 tokens that a
+// ones operand would cost (every tcgen05.mma takes ~100 cycles at N <= 64).
 __global__ void __launch_bounds__(192, 1)
     poly_update_kernel(const __grid_constant__ CUtensorMap tmKt, const __grid_constant__ CUtensorMap tmV,
                        const PolyParams p) {
@@ -294,8 +291,7 @@ __global__ void __launch_bounds__(192, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sKV = smem;                                  // stage: K^T 2 x 8 KB | V 16 KB
-  uint8_t* sOnes = sKV + kUpdStages * 32768;            // 4 KB
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sOnes + 4096);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sKV + kUpdStages * 32768);
   uint64_t* kv_full = bars;
   uint64_t* kv_empty = kv_full + kUpdStages;
   uint64_t* phi_full = kv_empty + kUpdStages;
@@ -311,14 +307,13 @@ __global__ void __launch_bounds__(192, 1)
     for (int i = 0; i < 2; ++i) { mbar_init(d_full + i, 1); mbar_init(d_empty + i, 128); }
     fence_mbar_init();
   }
-  if (warp >= 2) init_ones_tile(sOnes, threadIdx.x - 64, 128);
   if (warp == 1) { tmem_alloc(tmem_slot, 512); tmem_relinquish(); }
   fence_async_smem();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  // TMEM: deltas [0, 128) [128, 256) (N = 64 + 16 each) | phi_k [256, 320) [320, 384)
+  // TMEM: deltas [0, 64) [128, 192) | phi_k [256, 320) [320, 384)
   const uint32_t t_phi = tmem + 256;
   const int row0 = bh * p.S;
 
@@ -338,8 +333,6 @@ __global__ void __launch_bounds__(192, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idesc_v = idesc_f16_f32(128, 64, false, true);   // A from TMEM, B (V) MN-major
-      constexpr uint32_t idesc_1 = idesc_f16_f32(128, 16, false, false);  // B (ones) K-major
-      const uint32_t ones = smem_u32(sOnes);
       bool ok = true;
       for (int u = 0; u < n_sub && ok; ++u) {
         const int st = u % kUpdStages, pb = u % kUpdPhiBufs;
@@ -354,9 +347,7 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks) {  // K = 128 tokens, 16 per MMA (8 TMEM columns)
           const uint64_t bv = smem_desc(vv + ks * 2048, 8192, 1024, 128);
-          const uint64_t b1 = smem_desc(ones + (ks >> 2) * 2048 + (ks & 3) * 32, 16, 1024, 128);
           umma_f16_ts(d, phi + ks * 8, bv, idesc_v, ((u & 3) | ks) != 0);
-          umma_f16_ts(d + 64, phi + ks * 8, b1, idesc_1, ((u & 3) | ks) != 0);
         }
         umma_commit(kv_empty + st);
         umma_commit(phi_empty + pb);
@@ -373,13 +364,19 @@ __global__ void __launch_bounds__(192, 1)
     float state[65];
 #pragma unroll
     for (int n = 0; n < 65; ++n) state[n] = 0.f;
+    float den_chunk = 0.f, den_prev = 0.f;  // row sums of the chunk being built / awaiting drain
     bool ok = true;
     for (int u = 0; u < n_sub && ok; ++u) {
       const int st = u % kUpdStages, pb = u % kUpdPhiBufs;
+      if ((u & 3) == 0) {
+        den_prev = den_chunk;
+        den_chunk = 0.f;
+      }
       if (!mbar_wait(kv_full + st, (u / kUpdStages) & 1, p.err, kErrPolyWait)) { ok = false; break; }
       if (!mbar_wait(phi_empty + pb, ((u / kUpdPhiBufs) & 1) ^ 1, p.err, kErrPolyWait)) { ok = false; break; }
       tc_fence_after();
       const uint8_t* kt_st = sKV + st * 32768;
+      float dsum[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {  // tokens 64*hh .. +63 -> TMEM columns 32*hh .. +31
         uint32_t w[32];
@@ -397,19 +394,29 @@ __global__ void __launch_bounds__(192, 1)
           for (int e = 0; e < 32; ++e) w[e] = fill;
         }
         tmem_st32(t_phi + pb * 64 + hh * 32 + lane_off, w);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {  // the row's denominator contribution, FP32
+          unsigned short lo, hi;
+          asm("mov.b32 {%0, %1}, %2;" : "=h"(lo), "=h"(hi) : "r"(w[e]));
+          asm("add.rn.f32.f16 %0, %1, %2;" : "=f"(dsum[e & 3]) : "h"(lo), "f"(dsum[e & 3]));
+          asm("add.rn.f32.f16 %0, %1, %2;" : "=f"(dsum[e & 3]) : "h"(hi), "f"(dsum[e & 3]));
+        }
       }
+      den_chunk += (dsum[0] + dsum[1]) + (dsum[2] + dsum[3]);
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(phi_full + pb);
       mbar_arrive(kv_empty + st);  // K^T rows read (the MMA commit covers V)
       // drain the previous chunk's delta once this chunk's first sub-chunk is queued
       if ((u & 3) == 0 && u >= 4 &&
-          !update_drain(p, tmem, quarter, frow, fb, bh, (u >> 2) - 1, n_chunks, d_full, d_empty, coef, state)) {
+          !update_drain(p, tmem, quarter, frow, fb, bh, (u >> 2) - 1, n_chunks, d_full, d_empty, coef, den_prev,
+                        state)) {
         ok = false;
         break;
       }
     }
-    if (ok) update_drain(p, tmem, quarter, frow, fb, bh, (n_sub >> 2) - 1, n_chunks, d_full, d_empty, coef, state);
+    if (ok)
+      update_drain(p, tmem, quarter, frow, fb, bh, (n_sub >> 2) - 1, n_chunks, d_full, d_empty, coef, den_chunk, state);
   }
   tc_fence_before();
   __syncthreads();
@@ -422,7 +429,7 @@ constexpr int kAppSnapStages = 6;  // snapshot K-block ring (2 x [80 x 64] fp16 
 constexpr int kAppSnapBytes = 20480;
 constexpr int kAppPhiBufs = 2;     // phi_q feature blocks, in TMEM
 constexpr int kAppSmem = 16384 /*Q*/ + 2 * 32768 /*diag K,V ring*/ + kAppSnapStages * kAppSnapBytes +
-                         4096 /*ones*/ + 1024 + 256;
+                         1024 + 256;
 
 __global__ void __launch_bounds__(192, 1)
     poly_apply_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -441,8 +448,7 @@ __global__ void __launch_bounds__(192, 1)
   uint8_t* sQ = smem;
   uint8_t* sKV = sQ + 16384;                              // [2][K 16 KB | V 16 KB] -> 2 x 32 KB
   uint8_t* sSnap = sKV + 2 * 32768;
-  uint8_t* sOnes = sSnap + kAppSnapStages * kAppSnapBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sOnes + 4096);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sSnap + kAppSnapStages * kAppSnapBytes);
   uint64_t* q_full = bars;
   uint64_t* sn_full = q_full + 1;
   uint64_t* sn_empty = sn_full + kAppSnapStages;
@@ -467,7 +473,6 @@ __global__ void __launch_bounds__(192, 1)
     mbar_init(inter_done, 1);
     fence_mbar_init();
   }
-  if (warp >= 2) init_ones_tile(sOnes, threadIdx.x - 64, 128);
   if (warp == 1) { tmem_alloc(tmem_slot, 512); tmem_relinquish(); }
   fence_async_smem();
   tc_fence_before();
@@ -504,8 +509,6 @@ __global__ void __launch_bounds__(192, 1)
       constexpr uint32_t idesc_inter = idesc_f16_f32(128, kPolyN, false, false);
       constexpr uint32_t idesc_s = idesc_f16_f32(128, 128, false, false);
       constexpr uint32_t idesc_pv = idesc_f16_f32(128, 64, false, true);
-      constexpr uint32_t idesc_p1 = idesc_f16_f32(128, 16, false, false);
-      const uint32_t ones = smem_u32(sOnes);
       bool ok = true;
       // phase 1: inter = phi_q(q) @ S_c over 33 feature blocks; phi_q is the
       // TMEM A operand (TS form), so only the snapshot passes through smem
@@ -547,9 +550,7 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks) {
           const uint64_t bv = smem_desc(va + ks * 2048, 8192, 1024, 128);
-          const uint64_t b1 = smem_desc(ones + (ks >> 2) * 2048 + (ks & 3) * 32, 16, 1024, 128);
           umma_f16_ts(t_diag, t_p + ks * 8, bv, idesc_pv, (j | ks) != 0);
-          umma_f16_ts(t_diag + 64, t_p + ks * 8, b1, idesc_p1, (j | ks) != 0);
         }
         umma_commit(pv_done);
         umma_commit(kv_empty + st);
@@ -588,7 +589,7 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_before();
       mbar_arrive(phi_full + pb);
     }
-    const int qpos = (sblk * 128) + r;  // query position inside the chunk
+    float diag_den = 0.f;  // this query's sum of exp over the diagonal block
     for (int j = 0; j < n_diag && ok; ++j) {
       if (!mbar_wait(s_full, j & 1, p.err, kErrPolyWait)) { ok = false; break; }
       tc_fence_after();
@@ -606,6 +607,7 @@ __global__ void __launch_bounds__(192, 1)
         float v1 = fminf(__uint_as_float(s[2 * i + 1]) * sl2, kPolyMaxScore * 1.4426950408889634f);
         const float p0 = (2 * i <= lim) ? fast_exp2(v0) : 0.f;
         const float p1 = (2 * i + 1 <= lim) ? fast_exp2(v1) : 0.f;
+        diag_den += p0 + p1;
         s[i] = pack_half2(p0, p1);
       }
       tmem_st32(t_p + lane_off, *reinterpret_cast<uint32_t(*)[32]>(s));
@@ -615,7 +617,6 @@ __global__ void __launch_bounds__(192, 1)
       mbar_arrive(p_full);
       // the next S overwrites the S columns only after PV(j) (waited by the MMA thread)
     }
-    (void)qpos;
     if (ok && mbar_wait(inter_done, 0, p.err, kErrPolyWait) &&
         (n_diag == 0 || mbar_wait(pv_done, (n_diag - 1) & 1, p.err, kErrPolyWait))) {
       tc_fence_after();
@@ -626,11 +627,10 @@ __global__ void __launch_bounds__(192, 1)
       tmem_ld32(t_diag + lane_off, d0);
       tmem_ld32(t_diag + lane_off + 32, d1);
       tmem_ld_wait();
-      uint32_t e[32], f[32];
+      uint32_t e[32];
       tmem_ld32(t_inter + lane_off + 64, e);
-      tmem_ld32(t_diag + lane_off + 64, f);
       tmem_ld_wait();
-      const float den = t_prev * __uint_as_float(e[0]) + __uint_as_float(f[0]);
+      const float den = t_prev * __uint_as_float(e[0]) + diag_den;
       const float inv = 1.0f / den;
       const int qrow = u * 128 + r;
       __half* dst = p.ctx + ((size_t)b * p.S + qrow) * p.d_model + (size_t)h * 64;
