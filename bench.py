@@ -55,6 +55,7 @@ NCU_TRAFFIC_BYTES: dict = {
     ("C1", "attention"): 2632192 + 0,               # attn_fwd_persistent_kernel<32>
     ("C2", "attention"): 141639936 + 29552896,      # attn_fwd_kernel<64>
     ("C3", "gemm_ffn_in"): 57665792 + 168056064,    # gemm_tc_kernel<256,1>
+    ("C4", "attention"): 1780000000 + 576210000,    # attn_fwd_kernel<64>
 }
 CPU_DENSE_MAX = 8192  # longest sample the CPU baseline runs through the dense model
 
