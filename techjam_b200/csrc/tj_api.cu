@@ -303,7 +303,7 @@ int launch_layernorm(const float* x, const float* g, const float* b, void* out, 
 
 int launch_prepare(const uint8_t* mask, int B, int S, int* lengths, uint8_t* general, int* tile_list, int* n_live,
                    uint8_t* tile_live, cudaStream_t st) {
-  tj::prep_lengths_kernel<<<B, 256, 0, st>>>(mask, S, lengths, general);
+  tj::prep_lengths_kernel<<<B, 1024, 0, st>>>(mask, S, lengths, general);
   TJ_CUDA(cudaGetLastError());
   tj::prep_tiles_kernel<<<1, 1024, 0, st>>>(lengths, B, S, tile_list, n_live, tile_live);
   TJ_CUDA(cudaGetLastError());

@@ -9,8 +9,9 @@ constexpr int kTileRows = 128;
 
 // Per sample: length = 1 + last valid position (0 if none); general = mask is
 // not a right-padded prefix.  mask == null means every position is valid.
-__global__ void prep_lengths_kernel(const uint8_t* __restrict__ mask, int S, int* __restrict__ lengths,
-                                    uint8_t* __restrict__ general) {
+__global__ void __launch_bounds__(1024) prep_lengths_kernel(const uint8_t* __restrict__ mask, int S,
+                                                             int* __restrict__ lengths,
+                                                             uint8_t* __restrict__ general) {
   const int b = blockIdx.x;
   if (mask == nullptr) {
     if (threadIdx.x == 0) { lengths[b] = S; general[b] = 0; }
@@ -18,8 +19,23 @@ __global__ void prep_lengths_kernel(const uint8_t* __restrict__ mask, int S, int
   }
   const uint8_t* m = mask + (size_t)b * S;
   int last = 0, count = 0;
-  for (int i = threadIdx.x; i < S; i += blockDim.x) {
-    if (m[i]) { last = i + 1; ++count; }
+  if ((S & 15) == 0 && (reinterpret_cast<uintptr_t>(m) & 15) == 0) {
+    // 16 mask bytes per load; per byte: nonzero = valid
+    const uint4* m16 = reinterpret_cast<const uint4*>(m);
+    for (int i = threadIdx.x; i < S / 16; i += blockDim.x) {
+      const uint4 w = m16[i];
+      const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint32_t nz = __vcmpne4(words[q], 0u);  // 0xff per valid byte
+        count += __popc(nz) >> 3;
+        if (nz) last = 16 * i + 4 * q + 4 - (__clz(nz) >> 3);
+      }
+    }
+  } else {
+    for (int i = threadIdx.x; i < S; i += blockDim.x) {
+      if (m[i]) { last = i + 1; ++count; }
+    }
   }
   __shared__ int s_last[32], s_count[32];
   for (int o = 16; o > 0; o >>= 1) {
