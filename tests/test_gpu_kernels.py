@@ -137,6 +137,9 @@ def _attn_ref(q, k, v, mask, causal):
     (2, 4, 384, 64, True, "prefix"), (2, 2, 300, 32, True, "prefix"), (1, 2, 256, 128, True, "prefix"),
     (2, 4, 384, 64, False, "prefix"), (2, 3, 250, 64, True, "general"), (2, 2, 200, 64, False, "general"),
     (1, 16, 2048, 64, True, "none"), (3, 2, 1000, 128, False, "prefix"),
+    # more than two query-tile pairs at head_dim 64: the per-pair (column-split) kernel
+    (2, 4, 700, 64, True, "prefix"), (2, 3, 640, 64, True, "general"), (2, 2, 600, 64, False, "general"),
+    (2, 2, 777, 64, False, "prefix"), (3, 2, 1100, 64, True, "none"),
 ])
 def test_attention_matches_fp32(b, h, n, hd, causal, kind):
     gen = torch.Generator().manual_seed(b * 100 + n + hd)
