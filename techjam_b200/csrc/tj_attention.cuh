@@ -187,12 +187,12 @@ __global__ void __launch_bounds__(AttnCfg<HD>::kThreads, 1)
       }
     }
   } else if (warp == 9 || (Cfg::kPSeparate && warp == 10)) {
-    if (lane == 0) {
+    {  // the whole warp: every wait agrees in all lanes; tcgen05 issues come from the elected lane
       // ---------------------------------------------------------- MMA issuer(s)
       constexpr uint32_t idesc_qk = idesc_f16_f32(128, 128, false, false);
       constexpr uint32_t idesc_pv = idesc_f16_f32(128, HD, false, true);
       const uint32_t q_addr = smem_u32(sQ);
-      bool ok = mbar_wait(q_full, 0, p.err, kErrAttnMma);
+      bool ok = mbar_wait_warp(q_full, 0, p.err, kErrAttnMma);
       auto issue_s = [&](int t, int jj, uint32_t k_addr) {
         const uint32_t qa = q_addr + t * Cfg::kTile;
 #pragma unroll
@@ -201,9 +201,9 @@ __global__ void __launch_bounds__(AttnCfg<HD>::kThreads, 1)
           const int within = ((ks * 16) % Cfg::kAtomCols) * 2;
           const uint64_t ad = smem_desc(qa + atom * Cfg::kAtomBytes + within, 16, 8 * Cfg::kRowB, Cfg::kSw);
           const uint64_t bd = smem_desc(k_addr + atom * Cfg::kAtomBytes + within, 16, 8 * Cfg::kRowB, Cfg::kSw);
-          umma_f16_ss(tmem + Cfg::kColS + t * 128, ad, bd, idesc_qk, ks != 0);
+          umma_f16_ss_elect(tmem + Cfg::kColS + t * 128, ad, bd, idesc_qk, ks != 0);
         }
-        umma_commit(s_full + t);
+        umma_commit_elect(s_full + t);
       };
       auto issue_pv = [&](int t, int jj, uint32_t v_addr) {
         const uint32_t o_tmem = tmem + Cfg::kColO + t * HD;
@@ -211,10 +211,10 @@ __global__ void __launch_bounds__(AttnCfg<HD>::kThreads, 1)
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks) {
           const uint64_t bd = smem_desc(v_addr + ks * 16 * Cfg::kRowB, Cfg::kAtomBytes, 8 * Cfg::kRowB, Cfg::kSw);
-          umma_f16_ts(o_tmem, p_tmem + ks * 8, bd, idesc_pv, (jj | ks) != 0);
+          umma_f16_ts_elect(o_tmem, p_tmem + ks * 8, bd, idesc_pv, (jj | ks) != 0);
         }
-        umma_commit(pv_done + t);
-        if (jj == (t == 0 ? nkv0 : nkv1) - 1) umma_commit(o_final + t);
+        umma_commit_elect(pv_done + t);
+        if (jj == (t == 0 ? nkv0 : nkv1) - 1) umma_commit_elect(o_final + t);
       };
       auto kv_addr = [&](int jj) { return smem_u32(sKV + (jj % ST) * 2 * Cfg::kTile); };
       if constexpr (Cfg::kPSeparate) {
@@ -228,44 +228,44 @@ __global__ void __launch_bounds__(AttnCfg<HD>::kThreads, 1)
         const int nkv_t = t == 0 ? nkv0 : nkv1;
         for (int j = 0; j < n_kv && ok; ++j) {
           const int st = j % ST;
-          if (!mbar_wait(kv_full + st, (j / ST) & 1, p.err, kErrAttnMma)) { ok = false; break; }
+          if (!mbar_wait_warp(kv_full + st, (j / ST) & 1, p.err, kErrAttnMma)) { ok = false; break; }
           tc_fence_after();
           if (j >= nkv_t) {
-            mbar_arrive(kv_empty + st);
+            mbar_arrive_elect(kv_empty + st);
             continue;
           }
           if (j == 0) issue_s(t, 0, kv_addr(0));
           if (j + 1 < nkv_t) {
             const int sn = (j + 1) % ST;
-            if (!mbar_wait(kv_full + sn, ((j + 1) / ST) & 1, p.err, kErrAttnMma)) { ok = false; break; }
-            if (!mbar_wait(s_free + t, j & 1, p.err, kErrAttnMma)) { ok = false; break; }
+            if (!mbar_wait_warp(kv_full + sn, ((j + 1) / ST) & 1, p.err, kErrAttnMma)) { ok = false; break; }
+            if (!mbar_wait_warp(s_free + t, j & 1, p.err, kErrAttnMma)) { ok = false; break; }
             tc_fence_after();
             issue_s(t, j + 1, kv_addr(j + 1));
           }
-          if (!mbar_wait(p_full + t, j & 1, p.err, kErrAttnMma)) { ok = false; break; }
+          if (!mbar_wait_warp(p_full + t, j & 1, p.err, kErrAttnMma)) { ok = false; break; }
           tc_fence_after();
           issue_pv(t, j, kv_addr(j) + Cfg::kTile);
-          umma_commit(kv_empty + st);
+          umma_commit_elect(kv_empty + st);
         }
       } else {
         // P_t(j) lives in S_t's columns: S_t(j+1) must wait for PV_t(j).
         for (int j = 0; j < n_kv && ok; ++j) {
           const int st = j % ST;
-          if (!mbar_wait(kv_full + st, (j / ST) & 1, p.err, kErrAttnMma)) { ok = false; break; }
+          if (!mbar_wait_warp(kv_full + st, (j / ST) & 1, p.err, kErrAttnMma)) { ok = false; break; }
           tc_fence_after();
           for (int t = 0; t < 2 && ok; ++t) {
             if (j >= (t == 0 ? nkv0 : nkv1)) continue;
-            if (j > 0 && !mbar_wait(pv_done + t, (j - 1) & 1, p.err, kErrAttnMma)) { ok = false; break; }
+            if (j > 0 && !mbar_wait_warp(pv_done + t, (j - 1) & 1, p.err, kErrAttnMma)) { ok = false; break; }
             tc_fence_after();
             issue_s(t, j, kv_addr(j));
           }
           for (int t = 0; t < 2 && ok; ++t) {
             if (j >= (t == 0 ? nkv0 : nkv1)) continue;
-            if (!mbar_wait(p_full + t, j & 1, p.err, kErrAttnMma)) { ok = false; break; }
+            if (!mbar_wait_warp(p_full + t, j & 1, p.err, kErrAttnMma)) { ok = false; break; }
             tc_fence_after();
             issue_pv(t, j, kv_addr(j) + Cfg::kTile);
           }
-          umma_commit(kv_empty + st);
+          umma_commit_elect(kv_empty + st);
         }
       }
     }
@@ -511,7 +511,7 @@ __global__ void __launch_bounds__(AttnCfg<HD>::kThreadsPersist, 1)
       }
     }
   } else if (warp == 9 || warp == 10) {
-    if (lane == 0) {
+    {  // the whole warp: every wait agrees in all lanes; tcgen05 issues come from the elected lane
       // ---------------------------------------------------------- MMA issuers
       // Warp 9 issues query tile 0's S and PV, warp 10 tile 1's, each over the
       // same item sequence; both release every K/V stage and Q buffer (count
@@ -529,7 +529,7 @@ __global__ void __launch_bounds__(AttnCfg<HD>::kThreadsPersist, 1)
         if (!decode(i, it)) continue;
         const int qb = nitem & 1;
         const int nkv_t = t == 0 ? it.nkv0 : it.nkv1;
-        if (!mbar_wait(q_full + qb, (nitem >> 1) & 1, p.err, kErrAttnMma)) break;
+        if (!mbar_wait_warp(q_full + qb, (nitem >> 1) & 1, p.err, kErrAttnMma)) break;
         const uint32_t q_addr = smem_u32(sQ + qb * 2 * Cfg::kTile) + t * Cfg::kTile;
         auto kv_addr = [&](int j) { return smem_u32(sKV + ((kvc + j) % ST) * 2 * Cfg::kTile); };
         auto issue_s = [&](uint32_t k_addr) {
@@ -539,32 +539,32 @@ __global__ void __launch_bounds__(AttnCfg<HD>::kThreadsPersist, 1)
             const int within = ((ks * 16) % Cfg::kAtomCols) * 2;
             const uint64_t ad = smem_desc(q_addr + atom * Cfg::kAtomBytes + within, 16, 8 * Cfg::kRowB, Cfg::kSw);
             const uint64_t bd = smem_desc(k_addr + atom * Cfg::kAtomBytes + within, 16, 8 * Cfg::kRowB, Cfg::kSw);
-            umma_f16_ss(tmem + Cfg::kColS + t * 128, ad, bd, idesc_qk, ks != 0);
+            umma_f16_ss_elect(tmem + Cfg::kColS + t * 128, ad, bd, idesc_qk, ks != 0);
           }
-          umma_commit(s_full + t);
+          umma_commit_elect(s_full + t);
         };
         for (int j = 0; j < it.n_kv && ok; ++j) {
           const int g = kvc + j;
-          if (!mbar_wait(kv_full + g % ST, (g / ST) & 1, p.err, kErrAttnMma)) { ok = false; break; }
+          if (!mbar_wait_warp(kv_full + g % ST, (g / ST) & 1, p.err, kErrAttnMma)) { ok = false; break; }
           tc_fence_after();
           if (j >= nkv_t) {
-            mbar_arrive(kv_empty + g % ST);
+            mbar_arrive_elect(kv_empty + g % ST);
             continue;
           }
           if (j == 0) {  // S_t(0) once the previous item's last S_t has been read
-            if (cs > 0 && !mbar_wait(s_free + t, (cs - 1) & 1, p.err, kErrAttnMma)) { ok = false; break; }
+            if (cs > 0 && !mbar_wait_warp(s_free + t, (cs - 1) & 1, p.err, kErrAttnMma)) { ok = false; break; }
             tc_fence_after();
             issue_s(kv_addr(0));
           }
           if (j + 1 < nkv_t) {
             const int gn = g + 1;
-            if (!mbar_wait(kv_full + gn % ST, (gn / ST) & 1, p.err, kErrAttnMma)) { ok = false; break; }
-            if (!mbar_wait(s_free + t, (cs + j) & 1, p.err, kErrAttnMma)) { ok = false; break; }
+            if (!mbar_wait_warp(kv_full + gn % ST, (gn / ST) & 1, p.err, kErrAttnMma)) { ok = false; break; }
+            if (!mbar_wait_warp(s_free + t, (cs + j) & 1, p.err, kErrAttnMma)) { ok = false; break; }
             tc_fence_after();
             issue_s(kv_addr(j + 1));
           }
-          if (!mbar_wait(p_full + t, (cs + j) & 1, p.err, kErrAttnMma)) { ok = false; break; }
-          if (j == 0 && ci > 0 && !mbar_wait(o_free + t, (ci - 1) & 1, p.err, kErrAttnMma)) { ok = false; break; }
+          if (!mbar_wait_warp(p_full + t, (cs + j) & 1, p.err, kErrAttnMma)) { ok = false; break; }
+          if (j == 0 && ci > 0 && !mbar_wait_warp(o_free + t, (ci - 1) & 1, p.err, kErrAttnMma)) { ok = false; break; }
           tc_fence_after();
           const uint32_t o_tmem = tmem + Cfg::kColO + t * HD;
           const uint32_t p_tmem = tmem + Cfg::kColP + t * 64;
@@ -572,15 +572,15 @@ __global__ void __launch_bounds__(AttnCfg<HD>::kThreadsPersist, 1)
 #pragma unroll
           for (int ks = 0; ks < 8; ++ks) {
             const uint64_t bd = smem_desc(v_addr + ks * 16 * Cfg::kRowB, Cfg::kAtomBytes, 8 * Cfg::kRowB, Cfg::kSw);
-            umma_f16_ts(o_tmem, p_tmem + ks * 8, bd, idesc_pv, (j | ks) != 0);
+            umma_f16_ts_elect(o_tmem, p_tmem + ks * 8, bd, idesc_pv, (j | ks) != 0);
           }
-          umma_commit(pv_done + t);
-          if (j == nkv_t - 1) umma_commit(o_final + t);
-          umma_commit(kv_empty + g % ST);
+          umma_commit_elect(pv_done + t);
+          if (j == nkv_t - 1) umma_commit_elect(o_final + t);
+          umma_commit_elect(kv_empty + g % ST);
         }
         if (!ok) break;
-        if (nkv_t > 0) umma_commit(q_empty + qb);  // after this tile's S MMAs read Q
-        else mbar_arrive(q_empty + qb);
+        if (nkv_t > 0) umma_commit_elect(q_empty + qb);  // after this tile's S MMAs read Q
+        else mbar_arrive_elect(q_empty + qb);
         kvc += it.n_kv;
         cs += nkv_t;
         ci += nkv_t > 0 ? 1 : 0;

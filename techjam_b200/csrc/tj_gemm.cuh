@@ -326,7 +326,7 @@ __global__ void __launch_bounds__(320, 1)
         if (++stage == S) { stage = 0; phase ^= 1u; }
       }
     }
-  } else if (warp == 1 && lane == 0) {
+  } else if (warp == 1) {  // whole warp; tcgen05 issues from the elected lane
     // ------------------------------------------------------------ MMA issuer
     constexpr uint32_t idesc = idesc_f16_f32(kGemmBM, BN, false, false);
     int stage = 0;
@@ -335,11 +335,11 @@ __global__ void __launch_bounds__(320, 1)
     uint32_t aphase = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-      if (!mbar_wait(acc_empty + abuf, aphase ^ 1u, p.err, kErrGemmMma)) break;
+      if (!mbar_wait_warp(acc_empty + abuf, aphase ^ 1u, p.err, kErrGemmMma)) break;
       tc_fence_after();
       const uint32_t d_tmem = tmem_base + abuf * BN;
       for (int kb = 0; kb < k_blocks; ++kb) {
-        if (!mbar_wait(full + stage, phase, p.err, kErrGemmMma)) { ok = false; break; }
+        if (!mbar_wait_warp(full + stage, phase, p.err, kErrGemmMma)) { ok = false; break; }
         tc_fence_after();
         const uint32_t sa = smem_u32(smem + stage * Cfg::kStageBytes);
         const uint32_t sb = sa + Cfg::kStageA;
@@ -347,13 +347,13 @@ __global__ void __launch_bounds__(320, 1)
         for (int ks = 0; ks < kGemmBK / 16; ++ks) {
           const uint64_t ad = smem_desc(sa + ks * 32, 16, 1024, 128);
           const uint64_t bd = smem_desc(sb + ks * 32, 16, 1024, 128);
-          umma_f16_ss(d_tmem, ad, bd, idesc, (kb | ks) != 0);
+          umma_f16_ss_elect(d_tmem, ad, bd, idesc, (kb | ks) != 0);
         }
-        umma_commit(empty + stage);  // release the smem stage when these MMAs retire
+        umma_commit_elect(empty + stage);  // release the smem stage when these MMAs retire
         if (++stage == S) { stage = 0; phase ^= 1u; }
       }
       if (!ok) break;
-      umma_commit(acc_full + abuf);
+      umma_commit_elect(acc_full + abuf);
       if (++abuf == 2) { abuf = 0; aphase ^= 1u; }
     }
   } else if (warp >= 2) {
@@ -479,7 +479,7 @@ __global__ void __launch_bounds__(320, 1)
         if (++stage == S) { stage = 0; phase ^= 1u; }
       }
     }
-  } else if (warp == 1 && lane == 0 && rank == 0) {
+  } else if (warp == 1 && rank == 0) {  // whole warp; tcgen05 issues from the elected lane
     // ------------------------------------------------------------ 2-SM MMA issuer (even CTA)
     constexpr uint32_t idesc = idesc_f16_f32(256, BN, false, false);
     int stage = 0;
@@ -488,11 +488,11 @@ __global__ void __launch_bounds__(320, 1)
     uint32_t aphase = 0;
     bool ok = true;
     for (int t = pair; t < total && ok; t += n_pairs) {
-      if (!mbar_wait(acc_empty + abuf, aphase ^ 1u, p.err, kErrGemmMma)) break;
+      if (!mbar_wait_warp(acc_empty + abuf, aphase ^ 1u, p.err, kErrGemmMma)) break;
       tc_fence_after();
       const uint32_t d_tmem = tmem_base + abuf * BN;
       for (int kb = 0; kb < k_blocks; ++kb) {
-        if (!mbar_wait(full + stage, phase, p.err, kErrGemmMma)) { ok = false; break; }
+        if (!mbar_wait_warp(full + stage, phase, p.err, kErrGemmMma)) { ok = false; break; }
         tc_fence_after();
         const uint32_t sa = smem_u32(smem + stage * Cfg::kStageBytes);
         const uint32_t sb = sa + kGemmBM * kGemmBK * 2;
@@ -500,13 +500,13 @@ __global__ void __launch_bounds__(320, 1)
         for (int ks = 0; ks < kGemmBK / 16; ++ks) {
           const uint64_t ad = smem_desc(sa + ks * 32, 16, 1024, 128);
           const uint64_t bd = smem_desc(sb + ks * 32, 16, 1024, 128);
-          umma_f16_ss_pair(d_tmem, ad, bd, idesc, (kb | ks) != 0);
+          umma_f16_ss_pair_elect(d_tmem, ad, bd, idesc, (kb | ks) != 0);
         }
-        umma_commit_pair_both(empty + stage);
+        umma_commit_pair_both_elect(empty + stage);
         if (++stage == S) { stage = 0; phase ^= 1u; }
       }
       if (!ok) break;
-      umma_commit_pair_both(acc_full + abuf);
+      umma_commit_pair_both_elect(acc_full + abuf);
       if (++abuf == 2) { abuf = 0; aphase ^= 1u; }
     }
   } else if (warp >= 2) {

@@ -331,15 +331,15 @@ __global__ void __launch_bounds__(192, 1)
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    {  // the whole warp: every wait agrees in all lanes; tcgen05 issues come from the elected lane
       constexpr uint32_t idesc_v = idesc_f16_f32(128, 64, false, true);   // A from TMEM, B (V) MN-major
       bool ok = true;
       for (int u = 0; u < n_sub && ok; ++u) {
         const int st = u % kUpdStages, pb = u % kUpdPhiBufs;
         const int c = u >> 2, db = c & 1;
-        if ((u & 3) == 0 && !mbar_wait(d_empty + db, ((c >> 1) & 1) ^ 1, p.err, kErrPolyWait)) { ok = false; break; }
-        if (!mbar_wait(kv_full + st, (u / kUpdStages) & 1, p.err, kErrPolyWait)) { ok = false; break; }
-        if (!mbar_wait(phi_full + pb, (u / kUpdPhiBufs) & 1, p.err, kErrPolyWait)) { ok = false; break; }
+        if ((u & 3) == 0 && !mbar_wait_warp(d_empty + db, ((c >> 1) & 1) ^ 1, p.err, kErrPolyWait)) { ok = false; break; }
+        if (!mbar_wait_warp(kv_full + st, (u / kUpdStages) & 1, p.err, kErrPolyWait)) { ok = false; break; }
+        if (!mbar_wait_warp(phi_full + pb, (u / kUpdPhiBufs) & 1, p.err, kErrPolyWait)) { ok = false; break; }
         tc_fence_after();
         const uint32_t phi = t_phi + pb * 64;
         const uint32_t vv = smem_u32(sKV + st * 32768 + 16384);
@@ -347,11 +347,11 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks) {  // K = 128 tokens, 16 per MMA (8 TMEM columns)
           const uint64_t bv = smem_desc(vv + ks * 2048, 8192, 1024, 128);
-          umma_f16_ts(d, phi + ks * 8, bv, idesc_v, ((u & 3) | ks) != 0);
+          umma_f16_ts_elect(d, phi + ks * 8, bv, idesc_v, ((u & 3) | ks) != 0);
         }
-        umma_commit(kv_empty + st);
-        umma_commit(phi_empty + pb);
-        if ((u & 3) == 3) umma_commit(d_full + db);
+        umma_commit_elect(kv_empty + st);
+        umma_commit_elect(phi_empty + pb);
+        if ((u & 3) == 3) umma_commit_elect(d_full + db);
       }
     }
   } else {
@@ -505,7 +505,7 @@ __global__ void __launch_bounds__(192, 1)
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    {  // the whole warp: every wait agrees in all lanes; tcgen05 issues come from the elected lane
       constexpr uint32_t idesc_inter = idesc_f16_f32(128, kPolyN, false, false);
       constexpr uint32_t idesc_s = idesc_f16_f32(128, 128, false, false);
       constexpr uint32_t idesc_pv = idesc_f16_f32(128, 64, false, true);
@@ -514,46 +514,46 @@ __global__ void __launch_bounds__(192, 1)
       // TMEM A operand (TS form), so only the snapshot passes through smem
       for (int kb = 0; kb < kPolyFeatBlocks && ok; ++kb) {
         const int st = kb % kAppSnapStages, pb = kb % kAppPhiBufs;
-        if (!mbar_wait(sn_full + st, (kb / kAppSnapStages) & 1, p.err, kErrPolyWait)) { ok = false; break; }
-        if (!mbar_wait(phi_full + pb, (kb / kAppPhiBufs) & 1, p.err, kErrPolyWait)) { ok = false; break; }
+        if (!mbar_wait_warp(sn_full + st, (kb / kAppSnapStages) & 1, p.err, kErrPolyWait)) { ok = false; break; }
+        if (!mbar_wait_warp(phi_full + pb, (kb / kAppPhiBufs) & 1, p.err, kErrPolyWait)) { ok = false; break; }
         tc_fence_after();
         const uint32_t phi = t_phi + pb * 64;
         const uint32_t sn = smem_u32(sSnap + st * kAppSnapBytes);
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks) {  // K = 128 features, 16 per MMA (8 TMEM columns)
           const uint64_t bd = smem_desc(sn + (ks >> 2) * 10240 + (ks & 3) * 32, 16, 1024, 128);
-          umma_f16_ts(t_inter, phi + ks * 8, bd, idesc_inter, (kb | ks) != 0);
+          umma_f16_ts_elect(t_inter, phi + ks * 8, bd, idesc_inter, (kb | ks) != 0);
         }
-        umma_commit(sn_empty + st);
-        umma_commit(phi_empty + pb);
+        umma_commit_elect(sn_empty + st);
+        umma_commit_elect(phi_empty + pb);
       }
-      if (ok) umma_commit(inter_done);
+      if (ok) umma_commit_elect(inter_done);
       // phase 2: diagonal block, exact exp
-      if (ok && !mbar_wait(q_full, 0, p.err, kErrPolyWait)) ok = false;
+      if (ok && !mbar_wait_warp(q_full, 0, p.err, kErrPolyWait)) ok = false;
       const uint32_t qa = smem_u32(sQ);
       for (int j = 0; j < n_diag && ok; ++j) {
         const int st = j & 1;
-        if (!mbar_wait(kv_full + st, (j >> 1) & 1, p.err, kErrPolyWait)) { ok = false; break; }
-        if (j > 0 && !mbar_wait(pv_done, (j - 1) & 1, p.err, kErrPolyWait)) { ok = false; break; }
+        if (!mbar_wait_warp(kv_full + st, (j >> 1) & 1, p.err, kErrPolyWait)) { ok = false; break; }
+        if (j > 0 && !mbar_wait_warp(pv_done, (j - 1) & 1, p.err, kErrPolyWait)) { ok = false; break; }
         tc_fence_after();
         const uint32_t ka = smem_u32(sKV + st * 32768);
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks) {
           const uint64_t ad = smem_desc(qa + ks * 32, 16, 1024, 128);
           const uint64_t bd = smem_desc(ka + ks * 32, 16, 1024, 128);
-          umma_f16_ss(t_s, ad, bd, idesc_s, ks != 0);
+          umma_f16_ss_elect(t_s, ad, bd, idesc_s, ks != 0);
         }
-        umma_commit(s_full);
-        if (!mbar_wait(p_full, j & 1, p.err, kErrPolyWait)) { ok = false; break; }
+        umma_commit_elect(s_full);
+        if (!mbar_wait_warp(p_full, j & 1, p.err, kErrPolyWait)) { ok = false; break; }
         tc_fence_after();
         const uint32_t va = ka + 16384;
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks) {
           const uint64_t bv = smem_desc(va + ks * 2048, 8192, 1024, 128);
-          umma_f16_ts(t_diag, t_p + ks * 8, bv, idesc_pv, (j | ks) != 0);
+          umma_f16_ts_elect(t_diag, t_p + ks * 8, bv, idesc_pv, (j | ks) != 0);
         }
-        umma_commit(pv_done);
-        umma_commit(kv_empty + st);
+        umma_commit_elect(pv_done);
+        umma_commit_elect(kv_empty + st);
       }
     }
   } else {
