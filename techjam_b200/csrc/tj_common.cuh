@@ -119,27 +119,15 @@ TJ_DEV void tmem_dealloc(uint32_t taddr, uint32_t ncols) {  // whole warp
 TJ_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 TJ_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
-// D[tmem] (+)= A[smem] * B[smem], kind::f16 (fp16/bf16 in, fp32 accumulate).
-TJ_DEV void umma_f16_ss(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-// Arrive on an mbarrier once all previously issued tcgen05 ops of this thread complete.
-TJ_DEV void umma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
-}
-
-// The same issues made by the elected lane of a converged warp (elect.sync
-// picks the same lane every time while all 32 lanes are active, so the commit
-// tracks the MMAs that lane issued).  Measured on B200 with one CTA issuing 64
-// back-to-back M=128, K=16 MMAs: 104 cycles per instruction at N <= 128 and
-// 132 at N = 256 (SS form), against 148 and 175 when lane 0 issues alone
-// inside a divergent branch.
+// tcgen05 issues, made by the elected lane of a converged warp (elect.sync
+// picks the same lane every time while all 32 lanes are active, so a commit
+// tracks the MMAs that lane issued):
+//   umma_f16_ss_elect  D[tmem] (+)= A[smem] * B[smem], kind::f16 (fp16 in, fp32 accumulate)
+//   umma_f16_ts_elect  D[tmem] (+)= A[tmem] * B[smem]; A is M x 16 fp16 packed two per column
+//   umma_commit_elect  arrive on an mbarrier once the lane's issued tcgen05 ops complete
+// Measured on B200 with one CTA issuing 64 back-to-back M=128, K=16 MMAs:
+// 104 cycles per instruction at N <= 128 and 132 at N = 256 (SS form),
+// against 148 and 175 when lane 0 issues alone inside a divergent branch.
 TJ_DEV void umma_f16_ss_elect(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred e, p;\n\t.reg .b32 r;\n\t"
@@ -209,16 +197,9 @@ TJ_DEV void tmem_relinquish_pair() {
 TJ_DEV void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
   asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
 }
-// 2-SM MMA: D (M=256 split over the pair's TMEM) (+)= A (128 rows per CTA) * B (N/2 rows per CTA).
-TJ_DEV void umma_f16_ss_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-// Elected-lane forms of the two pair issues (see umma_f16_ss_elect).
+// Elected-lane 2-SM issues: D (M=256 split over the pair's TMEM) (+)= A (128
+// rows per CTA) * B (N/2 rows per CTA); the commit arrives on the barrier at
+// this offset in both CTAs of the pair once the pair's issued MMAs complete.
 TJ_DEV void umma_f16_ss_pair_elect(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                    uint32_t accumulate) {
   asm volatile(
@@ -235,15 +216,6 @@ TJ_DEV void umma_commit_pair_both_elect(uint64_t* bar) {
       "elect.sync r|e, 0xffffffff;\n\t"
       "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;\n\t}"
       ::"r"(smem_u32(bar)), "h"((uint16_t)0x3)
-      : "memory");
-}
-// Arrive on the barrier at this offset in both CTAs of the pair once the
-// pair's previously issued MMAs complete.
-TJ_DEV void umma_commit_pair_both(uint64_t* bar) {
-  asm volatile(
-      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
-          smem_u32(bar)),
-      "h"((uint16_t)0x3)
       : "memory");
 }
 
@@ -299,15 +271,6 @@ TJ_DEV void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
 }
 TJ_DEV void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
-// D[tmem] (+)= A[tmem] * B[smem], kind::f16; A is M x 16 fp16 packed two per column.
-TJ_DEV void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
 
 // 2^x on the SFU (PTX ex2.approx.ftz.f32; relative error ~2^-22).
 TJ_DEV float fast_exp2(float x) {
