@@ -670,18 +670,40 @@ __global__ void __launch_bounds__(192, 1)
 // snapshots.  gathered = every shard's total state [world][B*H][80][4224]
 // fp32; local snapshot c holds the mean over this shard's first 512c tokens;
 // afterwards it holds the mean over all tokens before its chunk.
-__global__ void poly_fixup_kernel(const float* __restrict__ gathered, int rank, int BH, __half* __restrict__ snap,
-                                  int n_snap, int prefix_chunks, float t_before) {
-  const size_t per = (size_t)kPolyN * kPolyFeat;
+__global__ void __launch_bounds__(256) poly_fixup_kernel(const float* __restrict__ gathered, int rank, int BH,
+                                                          __half* __restrict__ snap, int n_snap, int prefix_chunks,
+                                                          float t_before) {
+  // Eight consecutive state elements per thread: the earlier shards' sum is
+  // formed once (two float4 loads per shard), then every snapshot of those
+  // elements is rewritten with one 16-byte load and store.  Memory-bound:
+  // each rank reads and writes all of its snapshots once.
+  const size_t per = (size_t)kPolyN * kPolyFeat;  // a multiple of 8
   const size_t total = (size_t)BH * per;
-  for (size_t e = (size_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (size_t)gridDim.x * blockDim.x) {
-    float before = 0.f;
-    for (int r = 0; r < rank; ++r) before += gathered[(size_t)r * total + e];
+  const size_t per8 = per / 8;
+  for (size_t v = (size_t)blockIdx.x * blockDim.x + threadIdx.x; v < total / 8; v += (size_t)gridDim.x * blockDim.x) {
+    const size_t e = v * 8;
+    float before[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int r = 0; r < rank; ++r) {
+      const float4* g = reinterpret_cast<const float4*>(gathered + (size_t)r * total + e);
+      const float4 a = __ldg(g), b = __ldg(g + 1);
+      before[0] += a.x; before[1] += a.y; before[2] += a.z; before[3] += a.w;
+      before[4] += b.x; before[5] += b.y; before[6] += b.z; before[7] += b.w;
+    }
     const size_t bh = e / per, rem = e - bh * per;
+    uint4* sp = reinterpret_cast<uint4*>(snap + bh * n_snap * per + rem);
+#pragma unroll 4
     for (int i = 0; i < n_snap; ++i) {
-      __half* sp = snap + (bh * n_snap + i) * per + rem;
       const float t_loc = (float)((prefix_chunks + i) * kPolyChunk);
-      *sp = __float2half_rn((__half2float(*sp) * t_loc + before) / (t_loc + t_before));
+      const float inv = 1.0f / (t_loc + t_before);
+      uint4 w = sp[(size_t)i * per8];
+      uint32_t* h = reinterpret_cast<uint32_t*>(&w);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h[k]));
+        const __half2 o = __floats2half2_rn((f.x * t_loc + before[2 * k]) * inv, (f.y * t_loc + before[2 * k + 1]) * inv);
+        h[k] = *reinterpret_cast<const uint32_t*>(&o);
+      }
+      sp[(size_t)i * per8] = w;
     }
   }
 }
