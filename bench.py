@@ -53,7 +53,7 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 # kernel, from ncu captures of this build (profiles/*.md), keyed (workload, kernel class).
 NCU_TRAFFIC_BYTES: dict = {
     ("C1", "attention"): 2632192 + 0,               # attn_fwd_persistent_kernel<32>
-    ("C2", "attention"): 141639936 + 29552896,      # attn_fwd_kernel<64>
+    ("C2", "attention"): 141863424 + 32032768,      # attn_fwd_kernel<64>
     ("C3", "gemm_ffn_in"): 57665792 + 168056064,    # gemm_tc_kernel<256,1>
     ("C4", "attention"): 1780000000 + 576210000,    # attn_fwd_kernel<64>
 }
