@@ -448,9 +448,15 @@ def main():
     achieved = per_launch_flops / (per_launch_ms * 1e-3) / 1e12
     peak = peaks["bf16_tflops_sustained"]
     traffic = NCU_TRAFFIC_BYTES.get((wl.name, dom))
-    # exact-equivalent attention rate over everything attention-related (flash + polynomial route)
+    # attention rate per GPU: the tensor work this rank executed (flash kernel, plus the
+    # polynomial route's feature GEMMs when it ran) over the slowest rank's attention time;
+    # with the polynomial route also the exact-equivalent rate (exact causal flops of the
+    # whole job / time / GPUs), which is not bounded by the tensor peak
     attn_ms = kms_l[3] + kms_l[8]
-    attn_tflops = w_all["attn_flops"] / (attn_ms * 1e-3) / 1e12 if attn_ms > 0 else None
+    attn_exec = flops_of["attention"] + flops_of.get("poly", 0.0)
+    attn_tflops = attn_exec / (attn_ms * 1e-3) / 1e12 if attn_ms > 0 else None
+    attn_exact_eq = (w_all["attn_flops"] / (attn_ms * 1e-3) / 1e12 / world
+                     if attn_ms > 0 and "poly" in flops_of else None)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -480,6 +486,7 @@ def main():
             "throughput_tokens_per_s": round(w_all["tokens_valid"] / (ms * 1e-3), 1),
             "attn_tflops": None if attn_tflops is None else round(attn_tflops, 1),
             "attn_frac_of_peak": None if attn_tflops is None else round(attn_tflops / peak, 4),
+            "attn_tflops_exact_equivalent": None if attn_exact_eq is None else round(attn_exact_eq, 1),
             "gemm_tflops": round(w_all["gemm_flops"] / (ms * 1e-3) / 1e12, 1),
             "kernels": kernels,
             "roofline": {"kernel": dom, "bound": "tensor", "achieved": round(achieved, 1), "peak": peak,
