@@ -216,6 +216,59 @@ def run_reference(args):
     return 0
 
 
+def kernel_rates(cfg, lengths, my_lengths, kms_l, kcnt, steps, world, poly_prefix_here=True):
+    """Per-kernel-class rates of one timed pass.
+
+    ``kms_l``: ms per step of each libtj kernel class (max over ranks),
+    ``kcnt``: launches of each class over ``steps`` steps (this rank).
+    Returns the ``kernels`` table, the dominant tensor kernel class with its
+    per-launch achieved TFLOP/s, the attention rate per GPU (executed tensor
+    work: the flash kernel, plus the polynomial route's feature GEMMs when it
+    ran) and, with the polynomial route, the exact-equivalent attention rate
+    (exact causal flops of the whole job / time / GPUs), which the tensor peak
+    does not bound.
+    """
+    names = _lib.KERNEL_CLASSES
+    w_all = work(cfg, lengths)
+    w_mine = work(cfg, my_lengths)
+    flops_of = {"gemm_qkv": w_mine["gemm_qkv_flops"], "gemm_out": w_mine["gemm_out_flops"],
+                "gemm_ffn_in": w_mine["gemm_ffn_in_flops"], "gemm_ffn_out": w_mine["gemm_ffn_out_flops"],
+                "attention": w_mine["attn_flops"]}
+    poly_i, attn_i = names.index("poly"), names.index("attention")
+    if kcnt[poly_i]:
+        # polynomial route ran: the flash kernel only covered the 4096-token exact prefix, and the
+        # poly kernels issue 2*4224*80 tensor flops per key (update) and per query (apply)
+        bh = len(my_lengths) * cfg.num_heads
+        tok = sum(my_lengths) / max(1, len(my_lengths))
+        pre = min(4096, tok) if poly_prefix_here else 0
+        flops_of["attention"] = cfg.num_layers * 2.0 * cfg.d_model * len(my_lengths) * pre * (pre + 1)
+        flops_of["poly"] = cfg.num_layers * 2.0 * 4224 * 80 * bh * (2 * tok - pre)
+    total_k = sum(kms_l) or 1.0
+    kernels = {}
+    for i, n in enumerate(names):
+        if kcnt[i] == 0:
+            continue
+        entry = {"ms_per_step": round(kms_l[i], 4), "share": round(kms_l[i] / total_k, 4),
+                 "launches_per_step": kcnt[i] // steps}
+        if n in flops_of and kms_l[i] > 0:
+            entry["tflops"] = round(flops_of[n] / (kms_l[i] * 1e-3) / 1e12, 1)
+        kernels[n] = entry
+    dom = max((n for n in kernels if n in flops_of), key=lambda n: kernels[n]["ms_per_step"])
+    di = names.index(dom)
+    per_launch_ms = kms_l[di] / max(1, kcnt[di] // steps)
+    per_launch_flops = flops_of[dom] / max(1, kcnt[di] // steps)
+    attn_ms = kms_l[attn_i] + kms_l[poly_i]
+    attn_exec = flops_of["attention"] + flops_of.get("poly", 0.0)
+    return {
+        "kernels": kernels,
+        "dominant": dom,
+        "achieved": per_launch_flops / (per_launch_ms * 1e-3) / 1e12,
+        "attn_tflops": attn_exec / (attn_ms * 1e-3) / 1e12 if attn_ms > 0 else None,
+        "attn_exact_eq": (w_all["attn_flops"] / (attn_ms * 1e-3) / 1e12 / world
+                          if attn_ms > 0 and "poly" in flops_of else None),
+    }
+
+
 # ------------------------------------------------------------------ B200 arm
 def end_to_end(fwd, x, mask, steps, warmup, stream, barrier):
     """Per-step time of ``fwd`` fed from and drained to pinned host memory.
@@ -417,47 +470,13 @@ def main():
     # aggregate per-kernel timing across ranks (max ms per class)
     kms_l = [max_over_ranks(kms[i] / args.steps) for i in range(9)]
     peaks, peak_src = load_peaks()
-    w_all = work(cfg, lengths)
-    w_mine = work(cfg, my_lengths)
-    names = _lib.KERNEL_CLASSES
-    flops_of = {"gemm_qkv": w_mine["gemm_qkv_flops"], "gemm_out": w_mine["gemm_out_flops"],
-                "gemm_ffn_in": w_mine["gemm_ffn_in_flops"], "gemm_ffn_out": w_mine["gemm_ffn_out_flops"],
-                "attention": w_mine["attn_flops"]}
-    if kcnt[8]:
-        # polynomial route ran: the flash kernel only covered the 4096-token exact prefix, and the
-        # poly kernels issue 2*4224*80 tensor flops per key (update) and per query (apply)
-        bh = len(my_lengths) * cfg.num_heads
-        tok = sum(my_lengths) / max(1, len(my_lengths))
-        pre = min(4096, tok) if (not seqshard or rank == 0) else 0
-        flops_of["attention"] = cfg.num_layers * 2.0 * cfg.d_model * len(my_lengths) * pre * (pre + 1)
-        flops_of["poly"] = cfg.num_layers * 2.0 * 4224 * 80 * bh * (2 * tok - pre)
-    total_k = sum(kms_l) or 1.0
-    kernels = {}
-    for i, n in enumerate(names):
-        if kcnt[i] == 0:
-            continue
-        entry = {"ms_per_step": round(kms_l[i], 4), "share": round(kms_l[i] / total_k, 4),
-                 "launches_per_step": kcnt[i] // args.steps}
-        if n in flops_of and kms_l[i] > 0:
-            entry["tflops"] = round(flops_of[n] / (kms_l[i] * 1e-3) / 1e12, 1)
-        kernels[n] = entry
-    dom = max((n for n in kernels if n in flops_of), key=lambda n: kernels[n]["ms_per_step"])
-    di = names.index(dom)
-    per_launch_ms = kms_l[di] / max(1, kcnt[di] // args.steps)
-    per_launch_flops = flops_of[dom] / max(1, kcnt[di] // args.steps)
-    achieved = per_launch_flops / (per_launch_ms * 1e-3) / 1e12
     peak = peaks["bf16_tflops_sustained"]
+    rates = kernel_rates(cfg, lengths, my_lengths, kms_l, list(kcnt), args.steps, world,
+                         poly_prefix_here=(not seqshard or rank == 0))
+    kernels, dom = rates["kernels"], rates["dominant"]
+    achieved, attn_tflops, attn_exact_eq = rates["achieved"], rates["attn_tflops"], rates["attn_exact_eq"]
+    w_all = work(cfg, lengths)
     traffic = NCU_TRAFFIC_BYTES.get((wl.name, dom))
-    # attention rate per GPU: the tensor work this rank executed (flash kernel, plus the
-    # polynomial route's feature GEMMs when it ran) over the slowest rank's attention time;
-    # with the polynomial route also the exact-equivalent rate (exact causal flops of the
-    # whole job / time / GPUs), which is not bounded by the tensor peak
-    attn_ms = kms_l[3] + kms_l[8]
-    attn_exec = flops_of["attention"] + flops_of.get("poly", 0.0)
-    attn_tflops = attn_exec / (attn_ms * 1e-3) / 1e12 if attn_ms > 0 else None
-    attn_exact_eq = (w_all["attn_flops"] / (attn_ms * 1e-3) / 1e12 / world
-                     if attn_ms > 0 and "poly" in flops_of else None)
-
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cms, threads, idx, prefix = cpu_reference_ms(cfg, wl, x_full, mask_full, lengths, args.cpu_repeats, 1,
