@@ -490,7 +490,7 @@ int launch_poly_route(const __half* q, const __half* k, const __half* v, __half*
   }
   TJ_CHECK(timed_launch(m, TJ_K_POLY, 2, st, [&]() -> int { return launch_poly_update(pp, tv, st); }));
   TJ_CHECK(timed_launch(m, TJ_K_POLY, 1, st, [&]() -> int {
-    tj::poly_apply_kernel<<<dim3((n_chunks - pp.prefix_chunks) * 4, B * H), 192, tj::kAppSmem, st>>>(tq, tk, tv, tsn,
+    tj::poly_apply_kernel<<<dim3((n_chunks - pp.prefix_chunks) * 4, B * H), tj::kAppThreads, tj::kAppSmem, st>>>(tq, tk, tv, tsn,
                                                                                                    pp);
     TJ_CUDA(cudaGetLastError());
     return TJ_OK;
@@ -1029,7 +1029,7 @@ int shard_attention(TjModel* m, TjComm* cm, ShardWorkspace& w, int B, int S_loc,
         TJ_CUDA(cudaGetLastError());
       }
       TJ_CHECK(timed_launch(m, TJ_K_POLY, 1, st, [&]() -> int {
-        tj::poly_apply_kernel<<<dim3((n_chunks - pp.prefix_chunks) * 4, B * H), 192, tj::kAppSmem, st>>>(tq, tk, tv,
+        tj::poly_apply_kernel<<<dim3((n_chunks - pp.prefix_chunks) * 4, B * H), tj::kAppThreads, tj::kAppSmem, st>>>(tq, tk, tv,
                                                                                                        tsn, pp);
         TJ_CUDA(cudaGetLastError());
         return TJ_OK;

@@ -430,8 +430,13 @@ constexpr int kAppSnapBytes = 20480;
 constexpr int kAppPhiBufs = 2;     // phi_q feature blocks, in TMEM
 constexpr int kAppSmem = 16384 /*Q*/ + 2 * 32768 /*diag K,V ring*/ + kAppSnapStages * kAppSnapBytes +
                          1024 + 256;
+// warp 0 TMA; warps 1 and 2 issue the feature-block MMAs (even / odd blocks,
+// each into its own accumulator: a tcgen05.mma costs its issuing warp ~105
+// cycles however small N is, and two issuers halve that chain); warp 1 also
+// issues the diagonal block; warps 3..6 phi_q, diagonal exp and epilogue
+constexpr int kAppThreads = 224;
 
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kAppThreads, 1)
     poly_apply_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                       const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmSnap,
                       const PolyParams p) {
@@ -470,7 +475,7 @@ __global__ void __launch_bounds__(192, 1)
     mbar_init(s_full, 1);
     mbar_init(p_full, 128);
     mbar_init(pv_done, 1);
-    mbar_init(inter_done, 1);
+    mbar_init(inter_done, 2);  // both feature-block issuers
     fence_mbar_init();
   }
   if (warp == 1) { tmem_alloc(tmem_slot, 512); tmem_relinquish(); }
@@ -480,6 +485,9 @@ __global__ void __launch_bounds__(192, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   // TMEM: inter acc [0, 80) | diag acc [80, 160) | phi_q [160, 224) [224, 288) | S [288, 416) | P [416, 480)
+  // The odd feature blocks accumulate in the diag columns first; the epilogue
+  // warps move that partial to registers before they write the diagonal's P,
+  // so the diagonal P.V (which needs P) cannot overwrite it early.
   const uint32_t t_inter = tmem, t_diag = tmem + 80, t_phi = tmem + 160, t_s = tmem + 288, t_p = tmem + 416;
   const int row0 = bh * p.S;
   const int snap_row0 = (bh * (n_chunks - p.prefix_chunks) + (c - p.prefix_chunks)) * kPolyN;
@@ -504,15 +512,19 @@ __global__ void __launch_bounds__(192, 1)
         tma_load_2d(sKV + st * 32768 + 16384, &tmV, kv_full + st, 0, row0 + (c * 4 + j) * 128);
       }
     }
-  } else if (warp == 1) {
+  } else if (warp == 1 || warp == 2) {
     {  // the whole warp: every wait agrees in all lanes; tcgen05 issues come from the elected lane
       constexpr uint32_t idesc_inter = idesc_f16_f32(128, kPolyN, false, false);
       constexpr uint32_t idesc_s = idesc_f16_f32(128, 128, false, false);
       constexpr uint32_t idesc_pv = idesc_f16_f32(128, 64, false, true);
       bool ok = true;
       // phase 1: inter = phi_q(q) @ S_c over 33 feature blocks; phi_q is the
-      // TMEM A operand (TS form), so only the snapshot passes through smem
-      for (int kb = 0; kb < kPolyFeatBlocks && ok; ++kb) {
+      // TMEM A operand (TS form), so only the snapshot passes through smem.
+      // Warp 1 takes the even blocks (phi buffer 0) into the inter columns,
+      // warp 2 the odd ones (buffer 1) into the diag columns.
+      const int first_kb = warp - 1;
+      const uint32_t t_acc = warp == 1 ? t_inter : t_diag;
+      for (int kb = first_kb; kb < kPolyFeatBlocks && ok; kb += 2) {
         const int st = kb % kAppSnapStages, pb = kb % kAppPhiBufs;
         if (!mbar_wait_warp(sn_full + st, (kb / kAppSnapStages) & 1, p.err, kErrPolyWait)) { ok = false; break; }
         if (!mbar_wait_warp(phi_full + pb, (kb / kAppPhiBufs) & 1, p.err, kErrPolyWait)) { ok = false; break; }
@@ -522,13 +534,14 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks) {  // K = 128 features, 16 per MMA (8 TMEM columns)
           const uint64_t bd = smem_desc(sn + (ks >> 2) * 10240 + (ks & 3) * 32, 16, 1024, 128);
-          umma_f16_ts_elect(t_inter, phi + ks * 8, bd, idesc_inter, (kb | ks) != 0);
+          umma_f16_ts_elect(t_acc, phi + ks * 8, bd, idesc_inter, (kb != first_kb || ks != 0));
         }
         umma_commit_elect(sn_empty + st);
         umma_commit_elect(phi_empty + pb);
       }
       if (ok) umma_commit_elect(inter_done);
-      // phase 2: diagonal block, exact exp
+      // phase 2 (warp 1): diagonal block, exact exp
+      if (warp != 1) ok = false;
       if (ok && !mbar_wait_warp(q_full, 0, p.err, kErrPolyWait)) ok = false;
       const uint32_t qa = smem_u32(sQ);
       for (int j = 0; j < n_diag && ok; ++j) {
@@ -589,6 +602,20 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_before();
       mbar_arrive(phi_full + pb);
     }
+    // the odd feature blocks' partial (in the diag columns) -> registers
+    uint32_t b0[32], b1[32];
+    float den_b = 0.f;
+    if (ok && mbar_wait(inter_done, 0, p.err, kErrPolyWait)) {
+      tc_fence_after();
+      uint32_t e[32];
+      tmem_ld32(t_diag + lane_off, b0);
+      tmem_ld32(t_diag + lane_off + 32, b1);
+      tmem_ld32(t_diag + lane_off + 64, e);
+      tmem_ld_wait();
+      den_b = __uint_as_float(e[0]);
+    } else {
+      ok = false;
+    }
     float diag_den = 0.f;  // this query's sum of exp over the diagonal block
     for (int j = 0; j < n_diag && ok; ++j) {
       if (!mbar_wait(s_full, j & 1, p.err, kErrPolyWait)) { ok = false; break; }
@@ -617,8 +644,7 @@ __global__ void __launch_bounds__(192, 1)
       mbar_arrive(p_full);
       // the next S overwrites the S columns only after PV(j) (waited by the MMA thread)
     }
-    if (ok && mbar_wait(inter_done, 0, p.err, kErrPolyWait) &&
-        (n_diag == 0 || mbar_wait(pv_done, (n_diag - 1) & 1, p.err, kErrPolyWait))) {
+    if (ok && (n_diag == 0 || mbar_wait(pv_done, (n_diag - 1) & 1, p.err, kErrPolyWait))) {
       tc_fence_after();
       const float t_prev = p.t_before + (float)(c * kPolyChunk);
       uint32_t a0[32], a1[32], d0[32], d1[32];
@@ -630,7 +656,12 @@ __global__ void __launch_bounds__(192, 1)
       uint32_t e[32];
       tmem_ld32(t_inter + lane_off + 64, e);
       tmem_ld_wait();
-      const float den = t_prev * __uint_as_float(e[0]) + diag_den;
+      const float den = t_prev * (__uint_as_float(e[0]) + den_b) + diag_den;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {  // even + odd feature-block partials
+        a0[i] = __float_as_uint(__uint_as_float(a0[i]) + __uint_as_float(b0[i]));
+        a1[i] = __float_as_uint(__uint_as_float(a1[i]) + __uint_as_float(b1[i]));
+      }
       const float inv = 1.0f / den;
       const int qrow = u * 128 + r;
       __half* dst = p.ctx + ((size_t)b * p.S + qrow) * p.d_model + (size_t)h * 64;
