@@ -82,6 +82,8 @@ class _Handle:
 class B200Transformer(nn.Module):
     """Drop-in replacement for the reference ``BaselineTransformer`` forward."""
 
+    _MAX_GRAPHS = 8  # captured forwards kept per model (distinct input / mask tensors and shapes)
+
     def __init__(self, config, attention_route: str = "auto") -> None:
         super().__init__()
         if hasattr(config, "validate"):
@@ -171,7 +173,8 @@ class B200Transformer(nn.Module):
         return result
 
     def enable_cuda_graphs(self, enabled: bool = True) -> "B200Transformer":
-        """Replay the whole forward as one CUDA graph per (input, mask, shape).
+        """Replay the whole forward as one CUDA graph per (input, mask, shape),
+        keeping the eight most recently captured.
 
         The first call with given input/mask tensors runs normally, then
         captures the launch sequence; later calls with the SAME tensors
@@ -232,6 +235,8 @@ class B200Transformer(nn.Module):
                 after = ctypes.c_longlong()
                 _lib.call("tj_launch_count", handle.ptr, ctypes.byref(after))
                 entry = (graph, out, ws, int(after.value - before.value))
+                while len(self._graphs) >= self._MAX_GRAPHS:  # each entry pins its buffers: keep the newest
+                    self._graphs.pop(next(iter(self._graphs)))
                 self._graphs[key] = entry
             entry[0].replay()
             self.graph_kernel_launches += entry[3]
@@ -249,15 +254,3 @@ class B200Transformer(nn.Module):
             _lib.call("tj_device_error", self._handle.ptr, ctypes.byref(code))
         return int(code.value)
 
-
-def algorithmic_flops(config, lengths) -> Tuple[float, float]:
-    """(GEMM, exact-attention) flops over valid tokens: L*2*T_v*(4d^2+2dF) and
-    L*2*d*sum l(l+1) (causal) / L*4*d*sum l^2 (non-causal)."""
-    lengths = [int(v) for v in lengths]
-    L, d, F_ = config.num_layers, config.d_model, config.ffn_dim
-    gemm = L * 2.0 * sum(lengths) * (4 * d * d + 2 * d * F_)
-    if config.causal:
-        attn = L * 2.0 * d * sum(v * (v + 1) for v in lengths)
-    else:
-        attn = L * 4.0 * d * sum(v * v for v in lengths)
-    return gemm, attn
