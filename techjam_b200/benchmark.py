@@ -38,6 +38,7 @@ left to the bounded-memory oracle of the test suite.
 from __future__ import annotations
 
 import argparse
+import contextlib
 import importlib
 import importlib.util
 import json
@@ -56,7 +57,7 @@ import torch
 import torch.nn as nn
 
 from . import timing
-from .candidate import TransformerConfig
+from .candidate import TransformerConfig, validate_candidate_execution
 from .checker import AccuracyAccumulator
 from .harness import CONFIGS, generate_random_case
 
@@ -124,6 +125,8 @@ def parse_args(argv: Optional[List[str]] = None) -> argparse.Namespace:
                    help="'fp32' evaluates the baseline in true FP32 (TF32 off) during the accuracy "
                         "trials only; timing always uses the --allow-tf32 setting")
     p.add_argument("--baseline-per-sample", choices=("auto", "on", "off"), default="auto")
+    p.add_argument("--nvtx", action="store_true",
+                   help="annotate the timed region for Nsight Systems; adds profiling overhead")
     return p.parse_args(argv)
 
 
@@ -379,6 +382,13 @@ def memory_probe(models: Dict[str, nn.Module], x, mask, device) -> Optional[Dict
     return snaps
 
 
+def _nvtx_range(device, enabled: bool, label: str):
+    """An NVTX range for Nsight Systems when requested on CUDA (src/benchmark.py:249-252)."""
+    if not enabled or device.type != "cuda":
+        return contextlib.nullcontext()
+    return torch.cuda.nvtx.range(label)
+
+
 def _resolve_block_size(model, x, mask, device, args) -> int:
     if args.block_size > 0:
         return args.block_size
@@ -402,7 +412,8 @@ def paired_benchmark(baseline, candidate, cfg, device, x, mask, args) -> Dict[st
         block = _resolve_block_size(baseline, x, mask, device, args)
     runners = {timing.BASELINE: timing.make_block_runner(baseline, x, mask, device, block),
                timing.CANDIDATE: timing.make_block_runner(candidate, x, mask, device, block)}
-    samples = timing.measure_pair(runners, args.repeats, device=device)
+    with _nvtx_range(device, args.nvtx, "paired_timing"):
+        samples = timing.measure_pair(runners, args.repeats, device=device)
     summary = timing.paired_summary(samples)
     floor = timing.noise_floor_ratio(samples)
     significant = timing.is_significant(summary["speedup"], floor)
@@ -454,9 +465,10 @@ def legacy_benchmark(baseline, candidate, cfg, device, x, mask, args) -> Dict[st
     b_s: List[float] = []
     c_s: List[float] = []
     for r in range(args.benchmark_rounds):
-        order = [(baseline, b_s), (candidate, c_s)]
-        for model, dst in (order if r % 2 == 0 else order[::-1]):
-            dst.extend(_per_iteration_samples(model, x, mask, args.repeats, device))
+        order = [("baseline", baseline, b_s), ("candidate", candidate, c_s)]
+        for label, model, dst in (order if r % 2 == 0 else order[::-1]):
+            with _nvtx_range(device, args.nvtx, f"{label}_timed_round_{r + 1}"):
+                dst.extend(_per_iteration_samples(model, x, mask, args.repeats, device))
     tokens = cfg.batch_size * cfg.seq_len
     b_sum = _with_rates(timing.timing_summary(b_s), tokens)
     c_sum = _with_rates(timing.timing_summary(c_s), tokens)
@@ -499,6 +511,10 @@ def run(args: argparse.Namespace) -> int:
     spec = load_candidate(args.candidate)
     device = resolve_device(args.device)
     dtype = DTYPES[args.dtype]
+    validate_candidate_execution(
+        spec, args.case, dtype_name=args.dtype, input_scale=args.input_scale, device_type=device.type,
+        cuda_capability=torch.cuda.get_device_capability(device) if device.type == "cuda" else None,
+        torch_version=torch.__version__)
     torch.manual_seed(args.seed)
     torch.set_float32_matmul_precision(args.matmul_precision)
     if device.type == "cuda":
@@ -571,6 +587,7 @@ def run(args: argparse.Namespace) -> int:
         "config": asdict(cfg), "workload": args.workload, "official_case_id": args.case,
         "linear_scale": linear_scale, "dtype": args.dtype, "device": str(device),
         "padding_ratio": args.padding_ratio, "input_scale": args.input_scale, "seed": args.seed,
+        "nvtx_enabled": args.nvtx,
         "accuracy": accuracy, "performance": performance,
     }
     if args.output is not None:

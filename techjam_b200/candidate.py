@@ -1,7 +1,8 @@
 """Host-side mirror of the reference's candidate contract.
 
 ``CandidateSpec`` keeps the field names, defaults and validation rules of the
-reference's ``src/infra/candidate.py:15-130`` so that a module exposing
+reference's ``src/infra/candidate.py:15-130``, and ``validate_candidate_execution``
+its pre-allocation contract checks (:165-232), so that a module exposing
 ``CANDIDATE`` here can be consumed by the reference's loader
 (``load_candidate``, :133-162) once re-wrapped in its own class (see
 INTEGRATION.md for the two-line shim); ``TransformerConfig`` mirrors
@@ -91,3 +92,37 @@ class CandidateSpec:
         for _, cap in self.official_case_min_cuda_capability:
             if not (isinstance(cap, tuple) and len(cap) == 2 and all(isinstance(v, int) and v >= 0 for v in cap)):
                 raise TypeError("CUDA capabilities must be non-negative integer pairs")
+
+
+def validate_candidate_execution(spec: CandidateSpec, official_case_id: Optional[int], *, compile_user: bool = False,
+                                 dtype_name: Optional[str] = None, candidate_only: bool = False,
+                                 input_scale: float = 1.0, device_type: Optional[str] = None,
+                                 cuda_capability: Optional[Tuple[int, int]] = None,
+                                 torch_version: Optional[str] = None) -> None:
+    """Refuse a run that breaks the candidate's declared contract, before any
+    model or input is allocated (restates ``validate_candidate_execution``,
+    src/infra/candidate.py:165-232; same checks, same order)."""
+    if spec.self_compiling and compile_user:
+        raise ValueError(f"candidate {spec.name!r} compiles itself; remove --compile-user to avoid nested compilation")
+    if official_case_id in spec.unsupported_official_cases:
+        raise ValueError(f"candidate {spec.name!r} explicitly does not support official case {official_case_id}; "
+                         "refusing before model/input allocation")
+    dtypes = dict(spec.official_case_dtypes).get(official_case_id)
+    if dtypes is not None and dtype_name not in dtypes:
+        raise ValueError(f"candidate {spec.name!r} supports official case {official_case_id} only with "
+                         f"{', '.join(dtypes)}; received {dtype_name}; refusing before model/input allocation")
+    if official_case_id in spec.candidate_only_official_cases and not candidate_only:
+        raise ValueError(f"official case {official_case_id} has no runnable dense baseline; "
+                         "use the candidate-only runner")
+    if official_case_id in spec.default_input_scale_only_cases and input_scale != 1.0:
+        raise ValueError(f"official case {official_case_id} is validated only at the default input scale 1.0")
+    if official_case_id in spec.cuda_only_official_cases and device_type != "cuda":
+        raise ValueError(f"official case {official_case_id} requires CUDA; refusing before model/input allocation")
+    cap = dict(spec.official_case_min_cuda_capability).get(official_case_id)
+    if cap is not None and (cuda_capability is None or tuple(cuda_capability) < tuple(cap)):
+        raise ValueError(f"official case {official_case_id} requires CUDA capability {cap} or newer; "
+                         "refusing before model/input allocation")
+    versions = dict(spec.official_case_torch_versions).get(official_case_id)
+    if versions is not None and torch_version not in versions:
+        raise ValueError(f"official case {official_case_id} requires PyTorch {', '.join(versions)}; "
+                         "refusing before model/input allocation")

@@ -117,3 +117,36 @@ def test_loaders_and_baseline_modes(tmp_path):
     assert benchmark.dense_score_bytes(c4, 1) < 10e9 < benchmark.dense_score_bytes(c4, 64)
     args = benchmark.parse_args([])
     assert benchmark.baseline_mode(args, c4, torch.device("cpu")) == "per-sample"
+
+
+def test_candidate_contract_checked_before_allocation():
+    from techjam_b200.candidate import validate_candidate_execution
+
+    spec = CandidateSpec(name="c", model_factory=OracleEncoder, owner="t", description="d",
+                         unsupported_official_cases=(6,), official_case_dtypes=((8, ("float16",)),),
+                         candidate_only_official_cases=(14,), default_input_scale_only_cases=(13,),
+                         cuda_only_official_cases=(12,), official_case_min_cuda_capability=((11, (10, 0)),),
+                         official_case_torch_versions=((10, ("2.13.0",)),), self_compiling=True)
+    spec.validate()
+    validate_candidate_execution(spec, None)
+    validate_candidate_execution(spec, 8, dtype_name="float16")
+    for case, kwargs, what in [(6, {}, "does not support"), (8, {"dtype_name": "float32"}, "only with float16"),
+                               (14, {}, "no runnable dense baseline"), (13, {"input_scale": 2.0}, "input scale"),
+                               (12, {"device_type": "cpu"}, "requires CUDA"),
+                               (11, {"cuda_capability": (9, 0)}, "capability"),
+                               (10, {"torch_version": "2.11.0"}, "requires PyTorch"),
+                               (1, {"compile_user": True}, "compiles itself")]:
+        with pytest.raises(ValueError, match=what):
+            validate_candidate_execution(spec, case, **kwargs)
+    validate_candidate_execution(spec, 11, cuda_capability=(10, 0))
+
+
+def test_cli_refuses_a_declared_unsupported_case(capsys):
+    sys.modules["tjclitest.cands"].NO_CASE_2 = CandidateSpec(
+        name="no-case-2", model_factory=OracleEncoder, owner="tests", description="d",
+        unsupported_official_cases=(2,))
+    with pytest.raises(ValueError, match="does not support official case 2"):
+        benchmark.main(["--candidate", "tjclitest.cands:NO_CASE_2", *BASE, "--case", "2", "--device", "cpu"])
+    # --nvtx is accepted and is a no-op off the GPU
+    rc = benchmark.main(["--candidate", "tjclitest.cands", *BASE, *SMALL, "--nvtx"])
+    assert rc == 0
