@@ -18,6 +18,11 @@ Fixtures
                       ones), the generated input's checksum and lengths.
 ``poly_<name>.npz``   ``poly_linear_attention`` output (compute/state float32)
                       for seeded q/k/v, plus the guard's sigma estimate.
+``checker.npz`` +     the reference's ``compare_outputs`` verdicts (every field of
+``checker.json``      its ``AccuracyResult``) on deterministic edge cases, its
+                      ``percentile``, and the paired-timing statistics of
+                      ``src/infra/timing.py`` on fixed samples -- they pin the
+                      product-side checker and timing restatements.
 """
 
 from __future__ import annotations
@@ -117,8 +122,56 @@ def _poly_fixture(poly_ref, guard, name, spec):
                         sigma_est=np.float64(est), coeffs=np.array(c, dtype=np.float64))
 
 
+def _checker_cases():
+    """Deterministic (reference, candidate) pairs covering the criterion's edges."""
+    g = torch.Generator().manual_seed(7)
+    cases = {}
+    ref = torch.randn(2, 5, 7, generator=g)
+    cases["all_pass"] = (ref, ref + 1e-4 * torch.randn(2, 5, 7, generator=g))
+    got = ref + 1e-4 * torch.randn(2, 5, 7, generator=g)
+    got[1, 3, 4] += 0.25
+    got[0, 0, 2] += 0.01
+    cases["two_failures"] = (ref, got)
+    r = torch.tensor([[[1.0, 1.0, 0.01, 100.0, -0.5, 0.0]]])
+    c = torch.tensor([[[1.002, 1.0, 0.0121, 102.0, -0.5103, 0.0019]]])
+    cases["thresholds"] = (r, c)
+    got = ref.clone()
+    got[1, 2, 3] = float("nan")
+    cases["nan_candidate"] = (ref, got)
+    r2 = ref.clone()
+    r2[0, 4, 6] = float("inf")
+    cases["inf_reference"] = (r2, ref.clone())
+    return cases
+
+
+def _checker_fixture(ttb):
+    sys.path.insert(0, str(REF))
+    timing = importlib.import_module("src.infra.timing")
+    arrays, verdicts = {}, {}
+    for name, (r, c) in _checker_cases().items():
+        res = ttb.compare_outputs(r, c, rtol=0.02, atol=0.002)
+        arrays[f"{name}_ref"] = r.numpy()
+        arrays[f"{name}_cand"] = c.numpy()
+        verdicts[name] = {k: (list(v) if isinstance(v, tuple) else v) for k, v in vars(res).items()}
+    samples = {"baseline": [10.0, 12.0, 11.0, 13.0, 10.5, 12.5], "candidate": [5.0, 5.5, 5.2, 6.0, 5.1, 5.9]}
+    stats = {
+        "percentile": {str(q): ttb.percentile([3.0, 1.0, 4.0, 1.5, 9.0, 2.6], q) for q in (0.0, 0.5, 0.9, 1.0)},
+        "paired_schedule_5": timing.paired_schedule(5),
+        "samples": samples,
+        "paired_summary": timing.paired_summary(samples),
+        "paired_ratios": timing.paired_ratios(samples),
+        "noise_floor_ratio": timing.noise_floor_ratio(samples),
+        "choose_block_size": {str(ms): timing.choose_block_size(ms) for ms in (0.01, 0.3, 1.7, 5.0, 49.0, 80.0)},
+    }
+    np.savez_compressed(HERE / "checker.npz", **arrays)
+    (HERE / "checker.json").write_text(json.dumps({"verdicts": verdicts, "timing": stats}, indent=1,
+                                                  default=float) + "\n")
+
+
 def main():
     ttb, poly_ref, guard = _import_reference()
+    _checker_fixture(ttb)
+    print("checker")
     torch.set_num_threads(min(8, os.cpu_count() or 1))
     for name, spec in MODEL_CASES.items():
         _model_fixture(ttb, name, spec)
@@ -128,7 +181,8 @@ def main():
         print("poly", name)
     meta = {"reference_root": str(REF), "torch": torch.__version__,
             "model_cases": {k: list(v) for k, v in MODEL_CASES.items()},
-            "poly_cases": {k: list(v) for k, v in POLY_CASES.items()}}
+            "poly_cases": {k: list(v) for k, v in POLY_CASES.items()},
+            "checker_cases": sorted(_checker_cases())}
     (HERE / "MANIFEST.json").write_text(json.dumps(meta, indent=1) + "\n")
 
 
