@@ -6,7 +6,9 @@
 // reads it directly.
 //
 //   warp 8       TMA producer: both Q tiles once, then K/V tiles into a ring
-//   warp 9       one thread issues, per key tile j and query tile t:
+//   warps 9, 10  MMA issue (the elected lane of each converged warp), per
+//                key tile j, for query tile t = warp - 9 (head_dim <= 64;
+//                warp 9 issues both tiles for head_dim 128):
 //                  S_t = Q_t K_j^T          (SS form, fp32 in TMEM)
 //                  O_t += P_t V_j           (TS form: P_t read from TMEM)
 //   warps 0..3   softmax for query tile 0, warps 4..7 for tile 1: thread r

@@ -3,7 +3,7 @@
 //   C[M, N] = A[M, K] * W[N, K]^T     (A, W fp16 K-major; fp32 accumulate in TMEM)
 //
 // One CTA per SM.  Warp 0 issues TMA loads into a STAGES-deep shared-memory
-// ring, warp 1 (one thread) issues tcgen05.mma into one of two TMEM
+// ring, warp 1 (its elected lane) issues tcgen05.mma into one of two TMEM
 // accumulators, warps 2..9 drain the other accumulator through the epilogue
 // (tcgen05.ld -> bias / GELU / residual / head scatter -> shared-memory
 // transpose -> whole-line global stores).  Two epilogue warps share each TMEM
@@ -395,8 +395,8 @@ __global__ void __launch_bounds__(320, 1)
 // two live 128-row tiles (they need not be adjacent); an odd live count
 // leaves the last pair's second half reading the zero-filled rows past M.
 //   warp 0: TMA (both CTAs; completion on the even CTA's `full` barrier)
-//   warp 1: even CTA's single thread issues the 2-SM MMAs; commits are
-//           multicast to both CTAs (smem slot free / accumulator ready)
+//   warp 1: the even CTA's warp issues the 2-SM MMAs from its elected lane;
+//           commits are multicast to both CTAs (smem slot free / accumulator ready)
 //   warps 2..9: epilogue of this CTA's 128 rows; done -> even CTA's acc_empty
 struct Gemm2Cfg {
   static constexpr int kBN = 256;                       // N per pair tile (128 W rows per CTA)
