@@ -134,8 +134,23 @@ TJ_API int tj_forward_noalloc(TjModel* model, const float* x, const uint8_t* val
                               int seq_len, int route, void* stream);
 
 /* Reads (synchronously) and clears the model's device error word: 0 if no
-   kernel's bounded wait expired since the last call. */
+   kernel's bounded wait expired since the last call, else the site code of
+   the first wait that did (101-103 GEMM, 201-203 attention, 301 polynomial
+   route, 900 tj_wait_selftest). */
 TJ_API int tj_device_error(TjModel* model, int* code);
+
+/* Limit of every bounded wait in this library's kernels on the current
+   device, in nanoseconds of GPU global-timer time (0 restores the default,
+   4 s).  Applies to kernels launched after the call, for every model and
+   stream on the device.  Replaces no reference interface: the reference has
+   no device-side waits (its fallback contract is src/dispatcher.py:684-706). */
+TJ_API int tj_set_wait_limit(unsigned long long ns);
+/* Failure-path self-test (no counterpart in the reference): one warp waits on
+   a barrier that nothing completes, through the same bounded wait every
+   kernel uses; after the wait limit it records site code 900 in the model's
+   error word (model non-null) or in *err, and returns.  Nothing faults, traps
+   or hangs; the context stays usable. */
+TJ_API int tj_wait_selftest(TjModel* model, int* err, void* stream);
 
 /* ---- per-kernel timing (CUDA events recorded around each launch) ------- */
 
@@ -191,10 +206,13 @@ TJ_API int tj_gemm_f16(const void* a, const void* w, const float* bias, int batc
                 const int* n_live, const int* lengths, const uint8_t* mask, int* err, void* stream);
 
 /* ctx[B*S, H*hd] (fp16) = softmax(Q K^T * hd^-0.5 [+ causal/padding masks]) V
-   with Q,K,V fp16 [B,H,S,hd]; hd in {32, 64, 128}. */
+   with Q,K,V fp16 [B,H,S,hd]; hd in {32, 64, 128}.  sched (nullable): two
+   zero-filled ints through which the head_dim <= 64 kernel's CTAs claim work
+   items heavy-first; the kernel leaves them zero again.  Null: a static
+   round-robin assignment of the same items. */
 TJ_API int tj_attention_f16(const void* q, const void* k, const void* v, void* ctx, int batch, int heads, int seq_len,
                      int head_dim, int causal, const int* lengths, const uint8_t* mask, const uint8_t* general,
-                     int* err, void* stream);
+                     int* err, int* sched, void* stream);
 
 /* ---- sequence sharding over NCCL (one process per GPU) ----------------- */
 

@@ -14,6 +14,7 @@ from pathlib import Path
 LIB_PATH = Path(__file__).resolve().with_name("libtj.so")
 
 TJ_OK = 0
+TJ_ERR_DEVICE = 4
 STATUS_NAMES = {0: "TJ_OK", 1: "TJ_ERR_INVALID", 2: "TJ_ERR_UNSUPPORTED", 3: "TJ_ERR_CUDA",
                 4: "TJ_ERR_DEVICE", 5: "TJ_ERR_NO_DEVICE", 6: "TJ_ERR_NCCL"}
 ROUTE_EXACT, ROUTE_POLY, ROUTE_AUTO = 0, 1, 2
@@ -56,6 +57,8 @@ SIGNATURES = {
                            c_void_p]),
     "tj_forward_noalloc": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]),
     "tj_device_error": (c_int, [c_void_p, POINTER(c_int)]),
+    "tj_set_wait_limit": (c_int, [ctypes.c_ulonglong]),
+    "tj_wait_selftest": (c_int, [c_void_p, c_void_p, c_void_p]),
     "tj_profile_begin": (c_int, [c_void_p, c_int]),
     "tj_profile_end": (c_int, [c_void_p, POINTER(ctypes.c_double), POINTER(ctypes.c_longlong)]),
     "tj_launch_count": (c_int, [c_void_p, POINTER(ctypes.c_longlong)]),
@@ -76,7 +79,7 @@ SIGNATURES = {
     "tj_poly_attention_f16": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int,
                                       c_void_p, c_size_t, c_void_p, c_void_p]),
     "tj_attention_f16": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int,
-                                 c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
+                                 c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
 }
 
 _lock = threading.Lock()

@@ -114,13 +114,12 @@ const bool g_use_pair_gemm = [] {
   return !(e && e[0] == '0');
 }();
 
-// Persistent attention for head_dim <= 64: by default for sequences of at
-// most two query-tile pairs; TJ_ATTN_PERSIST=0 / 1 forces it off / on (A/B).
+// Persistent attention for head_dim <= 64 (the default); TJ_ATTN_PERSIST=0
+// selects the one-CTA-per-pair kernel instead (A/B comparisons).
 const int g_attn_persist = [] {
   const char* e = std::getenv("TJ_ATTN_PERSIST");
-  return (e && (e[0] == '0' || e[0] == '1')) ? e[0] - '0' : -1;
+  return (e && e[0] == '0') ? 0 : 1;
 }();
-constexpr int kPersistMaxPairs = 2;
 
 // ------------------------------------------------------------------ kernel launchers
 template <int BN, int EPI>
@@ -227,34 +226,53 @@ int launch_attn_hd(const void* q, const void* k, const void* v, const tj::AttnPa
   TJ_CHECK(make_map_f16(&tk, k, kv_rows, HD, 128, Cfg::kAtomCols, Cfg::kSw));
   TJ_CHECK(make_map_f16(&tv, v, kv_rows, HD, 128, Cfg::kAtomCols, Cfg::kSw));
   int dev = 0;
-  cudaGetDevice(&dev);
+  TJ_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fail(TJ_ERR_NO_DEVICE, "device index %d out of range", dev);
   const int q_tiles = (p.S + 127) / 128;
   const int n_pairs = (q_tiles + 1) / 2;
   bool persistent = false;
-  if constexpr (Cfg::kPSeparate)
-    persistent = g_attn_persist < 0 ? n_pairs <= kPersistMaxPairs : g_attn_persist == 1;
+  if constexpr (Cfg::kPSeparate) persistent = g_attn_persist != 0;
   if (persistent) {
     if constexpr (Cfg::kPSeparate) {
       // one CTA per SM over a heavy-first list of (pair, head, sample) items
-      static bool attr_set[64] = {};
+      using PC = tj::AttnPCfg<HD>;
       auto kern = tj::attn_fwd_persistent_kernel<HD>;
-      if (!attr_set[dev]) {
-        TJ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemPersist));
-        attr_set[dev] = true;
+      static std::mutex mu;
+      static bool checked[64] = {};
+      {
+        std::lock_guard<std::mutex> lock(mu);
+        if (!checked[dev]) {
+          // The kernel's per-warpgroup register budgets (setmaxnreg) add up to
+          // exactly the registers a 384-thread CTA is launched with; any other
+          // launch register count would leave the softmax warps waiting for
+          // registers that never free up, so refuse to launch instead.
+          cudaFuncAttributes fa;
+          TJ_CUDA(cudaFuncGetAttributes(&fa, kern));
+          if (fa.numRegs != PC::kRegLaunch)
+            return fail(TJ_ERR_UNSUPPORTED, "attention kernel built with %d registers per thread, needs %d",
+                        fa.numRegs, PC::kRegLaunch);
+          TJ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, PC::kSmemBytes));
+          checked[dev] = true;
+        }
       }
       DeviceInfo di;
       TJ_CHECK(device_info(&di));
       const long long items = (long long)n_pairs * B * p.H;
       if (items > 0x7fffffffLL - 2LL * di.sms) return fail(TJ_ERR_UNSUPPORTED, "too many attention work items");
       const int grid = (int)std::min<long long>(items, di.sms);
-      kern<<<grid, Cfg::kThreadsPersist, Cfg::kSmemPersist, st>>>(tq, tk, tv, p, n_pairs, (int)items);
+      if (grid <= 0) return TJ_OK;
+      kern<<<grid, PC::kThreads, PC::kSmemBytes, st>>>(tq, tk, tv, p, n_pairs);
     }
   } else {
+    static std::mutex mu;
     static bool attr_set[64] = {};
     auto kern = tj::attn_fwd_kernel<HD>;
-    if (!attr_set[dev]) {
-      TJ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes));
-      attr_set[dev] = true;
+    {
+      std::lock_guard<std::mutex> lock(mu);
+      if (!attr_set[dev]) {
+        TJ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes));
+        attr_set[dev] = true;
+      }
     }
     dim3 grid(n_pairs, B * p.H);  // one CTA per pair of 128-query tiles
     kern<<<grid, Cfg::kThreads, Cfg::kSmemBytes, st>>>(tq, tk, tv, p);
@@ -302,8 +320,8 @@ int launch_layernorm(const float* x, const float* g, const float* b, void* out, 
 }
 
 int launch_prepare(const uint8_t* mask, int B, int S, int* lengths, uint8_t* general, int* tile_list, int* n_live,
-                   uint8_t* tile_live, cudaStream_t st) {
-  tj::prep_lengths_kernel<<<B, 1024, 0, st>>>(mask, S, lengths, general);
+                   uint8_t* tile_live, int* sched, cudaStream_t st) {
+  tj::prep_lengths_kernel<<<B, 1024, 0, st>>>(mask, S, lengths, general, sched);
   TJ_CUDA(cudaGetLastError());
   tj::prep_tiles_kernel<<<1, 1024, 0, st>>>(lengths, B, S, tile_list, n_live, tile_live);
   TJ_CUDA(cudaGetLastError());
@@ -317,6 +335,7 @@ struct Workspace {
   int* tile_list;
   int* n_live;
   uint8_t* tile_live;
+  int* sched;   // attention work scheduler (2 ints, zeroed by the mask prep)
   __half* act;  // [M, d]: LN output, then attention context (reused)
   __half* q;
   __half* k;
@@ -359,6 +378,7 @@ size_t carve(const TjConfig& c, int B, int S, int route, uint8_t* base, Workspac
   t.tile_list = reinterpret_cast<int*>(take(sizeof(int) * tiles));
   t.n_live = reinterpret_cast<int*>(take(sizeof(int)));
   t.tile_live = take(tiles);
+  t.sched = reinterpret_cast<int*>(take(2 * sizeof(int)));
   t.act = reinterpret_cast<__half*>(take(2 * M * c.d_model));
   t.q = reinterpret_cast<__half*>(take(2 * M * c.d_model));
   t.k = reinterpret_cast<__half*>(take(2 * M * c.d_model));
@@ -472,6 +492,7 @@ int launch_poly_route(const __half* q, const __half* k, const __half* v, __half*
   tj::AttnParams ap = ap_in;
   ap.poly_admit = &ctl->admit;
   ap.exact_pairs = exact_prefix / 256;
+  if (ap.sched == nullptr) ap.sched = ctl->sched;
   TJ_CHECK(timed_launch(m, TJ_K_ATTN, 1, st, [&] { return launch_attention(q, k, v, 64, ap, B, st); }));
   const uint64_t rows = (uint64_t)B * H * S;
   CUtensorMap tq, tk, tv, tsn;
@@ -648,7 +669,7 @@ int tj_forward(TjModel* m, const float* x, const uint8_t* mask, float* out, int 
   const int M = B * S;
 
   TJ_CHECK(timed_launch(m, TJ_K_PREP, 2, st, [&] {
-    return launch_prepare(mask, B, S, w.lengths, w.general, w.tile_list, w.n_live, w.tile_live, st);
+    return launch_prepare(mask, B, S, w.lengths, w.general, w.tile_list, w.n_live, w.tile_live, w.sched, st);
   }));
   tj::RowValidity rv{w.lengths, mask, S, (long long)M};
 
@@ -676,6 +697,7 @@ int tj_forward(TjModel* m, const float* x, const uint8_t* mask, float* out, int 
   ap.kv_shard = S;
   ap.kv_shards = 1;
   ap.B = B;
+  ap.sched = w.sched;
 
   const float eps = c.layer_norm_eps;
   const float* resid_in = x;
@@ -835,6 +857,20 @@ int tj_profile_end(TjModel* m, double* ms, long long* counts) {
   return TJ_OK;
 }
 
+int tj_set_wait_limit(unsigned long long ns) {
+  const unsigned long long v = ns == 0 ? TJ_WAIT_NS : ns;
+  TJ_CUDA(cudaMemcpyToSymbol(tj::g_tj_wait_ns, &v, sizeof(v)));
+  return TJ_OK;
+}
+
+int tj_wait_selftest(TjModel* m, int* err, void* stream) {
+  int* word = m != nullptr ? m->err : err;
+  if (word == nullptr) return fail(TJ_ERR_INVALID, "need a model or an error word");
+  tj::wait_selftest_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(word);
+  TJ_CUDA(cudaGetLastError());
+  return TJ_OK;
+}
+
 int tj_launch_count(TjModel* m, long long* count) {
   if (!m || !count) return fail(TJ_ERR_INVALID, "null argument");
   *count = m->launches;
@@ -846,7 +882,8 @@ int tj_prepare_mask(const uint8_t* mask, int B, int S, int* lengths, uint8_t* ge
                     uint8_t* tile_live, void* stream) {
   if (!lengths || !general || !tile_list || !n_live || !tile_live) return fail(TJ_ERR_INVALID, "null argument");
   if (B <= 0 || S <= 0) return fail(TJ_ERR_INVALID, "batch and seq_len must be positive");
-  return launch_prepare(mask, B, S, lengths, general, tile_list, n_live, tile_live, static_cast<cudaStream_t>(stream));
+  return launch_prepare(mask, B, S, lengths, general, tile_list, n_live, tile_live, nullptr,
+                        static_cast<cudaStream_t>(stream));
 }
 
 int tj_layernorm(const float* x, const float* g, const float* b, int B, int S, int d, float eps, void* out,
@@ -883,7 +920,8 @@ int tj_gemm_f16(const void* a, const void* wgt, const float* bias, int B, int S,
 }
 
 int tj_attention_f16(const void* q, const void* k, const void* v, void* ctx, int B, int H, int S, int hd, int causal,
-                     const int* lengths, const uint8_t* mask, const uint8_t* general, int* err, void* stream) {
+                     const int* lengths, const uint8_t* mask, const uint8_t* general, int* err, int* sched,
+                     void* stream) {
   if (!q || !k || !v || !ctx || !lengths || !general || !err) return fail(TJ_ERR_INVALID, "null argument");
   DeviceInfo di;
   TJ_CHECK(device_info(&di));
@@ -896,6 +934,7 @@ int tj_attention_f16(const void* q, const void* k, const void* v, void* ctx, int
   p.kv_shard = S;
   p.kv_shards = 1;
   p.B = B;
+  p.sched = sched;
   return launch_attention(q, k, v, hd, p, B, static_cast<cudaStream_t>(stream));
 }
 
@@ -1139,6 +1178,7 @@ int tj_forward_seqshard(TjModel* m, TjComm* cm, const float* x, float* out, int 
     fill_int_kernel<<<(B + 255) / 256, 256, 0, st>>>(w.base.lengths, B, S_total);
     TJ_CUDA(cudaGetLastError());
     TJ_CUDA(cudaMemsetAsync(w.base.general, 0, B, st));
+    TJ_CUDA(cudaMemsetAsync(w.base.sched, 0, 2 * sizeof(int), st));
     tj::prep_tiles_kernel<<<1, 1024, 0, st>>>(w.base.lengths, B, S_loc, w.base.tile_list, w.base.n_live,
                                               w.base.tile_live);
     TJ_CUDA(cudaGetLastError());
@@ -1154,7 +1194,7 @@ int tj_forward_seqshard(TjModel* m, TjComm* cm, const float* x, float* out, int 
   ap.lengths = w.base.lengths; ap.mask = nullptr; ap.general = w.base.general; ap.ctx = w.base.act;
   ap.S = S_loc; ap.H = H; ap.d_model = d; ap.causal = 1;
   ap.scale_log2 = (float)(1.0 / std::sqrt((double)hd) * 1.4426950408889634);
-  ap.err = m->err; ap.B = B; ap.kv_shard = S_loc; ap.kv_shards = 1; ap.q_pos0 = 0;
+  ap.err = m->err; ap.B = B; ap.kv_shard = S_loc; ap.kv_shards = 1; ap.q_pos0 = 0; ap.sched = w.base.sched;
   const float eps = c.layer_norm_eps;
   const float* resid_in = x;
   for (int l = 0; l < c.num_layers; ++l) {

@@ -51,6 +51,10 @@ struct AttnParams {
   int kv_shard;
   int kv_shards;  // shards present in K/V (1 unless sharded)
   int B;
+  // Persistent kernel's work scheduler: {next item, CTAs finished}, zero
+  // before the launch and zero again after it (the last CTA to finish resets
+  // both).  Null: item i goes to CTA i % grid.
+  int* sched;
 };
 
 template <int HD>
@@ -64,7 +68,6 @@ struct AttnCfg {
   static constexpr int kTile = 128 * HD * 2;
   static constexpr int kStages = HD >= 128 ? 2 : (HD == 64 ? 4 : 6);
   static constexpr int kSmemBytes = 2 * kTile + kStages * 2 * kTile + 1024 + 256;
-  static constexpr int kSmemPersist = 4 * kTile + kStages * 2 * kTile + 1024 + 512;  // Q double-buffered
   static constexpr int kTmemCols = 512;
   // TMEM columns.  HD <= 64: S0 S1 (fp32) | P0 P1 (fp16 pairs) | O0 O1, so the
   // next S can be computed while P is still being consumed.  HD = 128: P
@@ -76,7 +79,6 @@ struct AttnCfg {
   // TMA warp 8, MMA warp 9, 8 softmax warps; with P in its own columns a
   // second MMA warp (10) issues tile 1's S and PV.
   static constexpr int kThreads = HD <= 64 ? 352 : 320;
-  static constexpr int kThreadsPersist = 352;  // TMA warp 8, MMA warps 9-10, 8 softmax warps
   static constexpr float kRescaleLog2 = 8.0f;
 };
 
@@ -378,66 +380,98 @@ __global__ void __launch_bounds__(AttnCfg<HD>::kThreads, 1)
 
 }  // namespace tj
 
+
 namespace tj {
 
-// ------------------------------------------------------------------ persistent variant
-// Same arithmetic as attn_fwd_kernel (head_dim <= 64, P in its own TMEM
-// columns), but one CTA per SM walks a heavy-first list of work items
-// (query-tile pair, head, sample) round-robin: item i covers pair
-// (np-1 - i/BH) of head-sample i%BH for causal attention, so the longest
-// items start first.  Every role decodes the same item sequence itself.
-// It pays off where items are short (a pair or two of query tiles per
-// sequence), which the one-CTA-per-pair grid spends on CTA start-up.
-// TMEM and barriers are set up once; Q is double-buffered so the next item's
-// Q and K/V stream in while the current one finishes, and every barrier phase
-// is tracked with running use counters across items.
+// ------------------------------------------------------------------ persistent warp-specialised kernel
+// Same arithmetic per (pair of 128-query tiles, head, sample) work item as
+// attn_fwd_kernel with head_dim <= 64 (P in its own TMEM columns), but one CTA
+// per SM walks the items heavy-first: item i covers query-tile pair
+// np-1 - i/BH of head-sample i%BH for causal attention.  With a scheduler
+// (AttnParams::sched) CTAs claim items with an atomic counter, so each SM
+// takes the next heaviest item when it frees up; without one CTA c takes
+// items c, c + grid, ...  Roles (12 warps, three warpgroups):
+//   warp 8       producer: claims the next live item, publishes it in a
+//                4-slot ring, loads its two Q tiles (double-buffered across
+//                items) and streams the K/V tiles through the stage ring
+//   warp 9       issues S_t = Q_t K_j^T for both query tiles (SS form)
+//   warps 10, 11 issue O_t += P_t V_j for query tile 0 / 1 (TS form)
+//   warps 0..7   softmax, warpgroup t for query tile t (thread = query row)
+// Three issuing warps keep the tensor pipe fed: a tcgen05.mma costs its
+// issuing warp ~100 cycles whatever its size, so one warp issuing a tile's
+// 4 + 8 MMAs per key tile serialises ~1.2k cycles of issue per step.  The
+// softmax warpgroups get 224 registers per thread (the 128-column score row
+// stays in registers, no spills) and the issuing warpgroup keeps 56:
+// 2 x 224 + 56 = 3 x 168, the launch's register share.
+// Item transitions overlap: the S issuer starts the next item's S_t(0) as
+// soon as the softmax has read the last S_t, and the softmax warps
+// exponentiate the next item's first key tile before they drain the previous
+// item's O_t (normalise, store) -- the drain waits for that item's last P.V,
+// which thereby runs under the exponentials.
 template <int HD>
-__global__ void __launch_bounds__(AttnCfg<HD>::kThreadsPersist, 1)
+struct AttnPCfg {
+  using Base = AttnCfg<HD>;
+  static constexpr int kThreads = 384;
+  static constexpr int kStages = HD == 64 ? 4 : 6;
+  static constexpr int kItemSlots = 4;
+  static constexpr int kRegLaunch = 168;  // 65536 / 384, rounded down to a multiple of 8
+  static constexpr int kRegSoftmax = 224;
+  static constexpr int kRegIssue = 56;
+  static_assert(2 * kRegSoftmax + kRegIssue == 3 * kRegLaunch, "register split must use the launch's registers");
+  static constexpr int kBarBytes = 8 * (14 + 2 * kStages + 2 * kItemSlots) + 4 * kItemSlots + 4;
+  static_assert(kBarBytes <= 512, "barrier region");
+  static constexpr int kSmemBytes = 4 * Base::kTile + kStages * 2 * Base::kTile + 1024 + 512;
+};
+
+template <int HD>
+__global__ void __launch_bounds__(384, 1)
     attn_fwd_persistent_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                               const __grid_constant__ CUtensorMap tmV, const AttnParams p, int n_pairs,
-                               int n_items) {
+                               const __grid_constant__ CUtensorMap tmV, const AttnParams p, int n_pairs) {
   using Cfg = AttnCfg<HD>;
-  static_assert(Cfg::kPSeparate, "persistent variant needs P in its own TMEM columns");
-  constexpr int ST = Cfg::kStages;
-  static_assert(8 * (16 + 2 * ST) + 4 <= 512, "barrier region exceeds its share of kSmemPersist");
-  if (error_raised(p.err)) return;
+  using PC = AttnPCfg<HD>;
+  static_assert(Cfg::kPSeparate, "persistent kernel needs P in its own TMEM columns");
+  constexpr int ST = PC::kStages;
+  constexpr int NI = PC::kItemSlots;
   const int BH = p.B * p.H;
   const bool gated = p.poly_admit != nullptr && *reinterpret_cast<const volatile int*>(p.poly_admit) != 0;
   // an admitted polynomial route leaves only the exact prefix's pairs here
   const int np = gated ? min(n_pairs, p.exact_pairs) : n_pairs;
-  n_items = np * BH;
+  const int n_items = np * BH;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;                         // [2 buffers][2 tiles][tile]
-  uint8_t* sKV = sQ + 4 * Cfg::kTile;         // stage s: K at s*2*kTile, V after it
+  uint8_t* sQ = smem;                      // [2 buffers][2 tiles][tile]
+  uint8_t* sKV = sQ + 4 * Cfg::kTile;      // stage s: K at s*2*kTile, V after it
   uint64_t* bars = reinterpret_cast<uint64_t*>(sKV + ST * 2 * Cfg::kTile);
-  uint64_t* q_full = bars;                    // [2]
-  uint64_t* q_empty = q_full + 2;             // [2]
-  uint64_t* kv_full = q_empty + 2;            // [ST]
-  uint64_t* kv_empty = kv_full + ST;          // [ST]
-  uint64_t* s_full = kv_empty + ST;           // [2 tiles]
+  uint64_t* q_full = bars;                 // [2]
+  uint64_t* q_empty = q_full + 2;          // [2]
+  uint64_t* kv_full = q_empty + 2;         // [ST]
+  uint64_t* kv_empty = kv_full + ST;       // [ST]
+  uint64_t* s_full = kv_empty + ST;        // [2 tiles]
   uint64_t* s_free = s_full + 2;
   uint64_t* p_full = s_free + 2;
   uint64_t* pv_done = p_full + 2;
   uint64_t* o_final = pv_done + 2;
-  uint64_t* o_free = o_final + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_free + 2);
+  uint64_t* item_full = o_final + 2;       // [NI]
+  uint64_t* item_empty = item_full + NI;   // [NI]
+  int* item_slot = reinterpret_cast<int*>(item_empty + NI);  // [NI]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(item_slot + NI);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    // Q buffers and K/V stages are released by both MMA issuers
-    for (int i = 0; i < 2; ++i) { mbar_init(q_full + i, 1); mbar_init(q_empty + i, 2); }
-    for (int i = 0; i < ST; ++i) { mbar_init(kv_full + i, 1); mbar_init(kv_empty + i, 2); }
+    for (int i = 0; i < 2; ++i) { mbar_init(q_full + i, 1); mbar_init(q_empty + i, 1); }
+    // each K/V stage is released by the S issuer and both P.V issuers
+    for (int i = 0; i < ST; ++i) { mbar_init(kv_full + i, 1); mbar_init(kv_empty + i, 3); }
     for (int i = 0; i < 2; ++i) {
       mbar_init(s_full + i, 1);
       mbar_init(s_free + i, 128);
       mbar_init(p_full + i, 128);
       mbar_init(pv_done + i, 1);
       mbar_init(o_final + i, 1);
-      mbar_init(o_free + i, 128);
     }
+    // an item slot is read by the 11 consumer warps (8 softmax, 3 issuers)
+    for (int i = 0; i < NI; ++i) { mbar_init(item_full + i, 1); mbar_init(item_empty + i, 11); }
     fence_mbar_init();
   }
   if (warp == 9) {
@@ -476,101 +510,142 @@ __global__ void __launch_bounds__(AttnCfg<HD>::kThreadsPersist, 1)
     const int shard = pos / p.kv_shard;
     return ((shard * p.B + it.b) * p.H + it.h) * p.kv_shard + (pos - shard * p.kv_shard);
   };
+  // Consumer side of the item ring (whole warp): the n-th published item, or
+  // -1 once the producer has run out of work.
+  auto next_item = [&](int n, int& item, int site) -> bool {
+    const int slot = n % NI;
+    if (!mbar_wait_warp(item_full + slot, (n / NI) & 1, p.err, site)) return false;
+    int v = 0;
+    if (lane == 0) v = *reinterpret_cast<volatile int*>(item_slot + slot);
+    item = __shfl_sync(0xffffffffu, v, 0);
+    mbar_arrive_elect(item_empty + slot);
+    return true;
+  };
 
-  if (warp == 8) {
-    if (lane == 0) {
-      // ---------------------------------------------------------- producer
-      tma_prefetch_desc(&tmQ);
-      tma_prefetch_desc(&tmK);
-      tma_prefetch_desc(&tmV);
-      int kvc = 0, nitem = 0;
-      bool ok = true;
-      for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x) {
-        Item it;
-        if (!decode(i, it)) continue;
-        const int qb = nitem & 1;
-        if (nitem >= 2 && !mbar_wait(q_empty + qb, ((nitem >> 1) - 1) & 1, p.err, kErrAttnProducer)) break;
-        mbar_expect_tx(q_full + qb, (it.has1 ? 2 : 1) * Cfg::kTile);
-        for (int t = 0; t < (it.has1 ? 2 : 1); ++t)
+  if (warp >= 8) {
+    reg_dealloc<PC::kRegIssue>();
+    if (warp == 8) {
+      if (lane == 0) {
+        // ---------------------------------------------------------- producer
+        tma_prefetch_desc(&tmQ);
+        tma_prefetch_desc(&tmK);
+        tma_prefetch_desc(&tmV);
+        int static_next = blockIdx.x;
+        auto claim = [&]() {
+          if (p.sched != nullptr) return atomicAdd(p.sched, 1);
+          const int c = static_next;
+          static_next += gridDim.x;
+          return c;
+        };
+        // the next claim is issued as soon as the current item is known, so
+        // its latency hides under this item's loads
+        int pending = error_raised(p.err) ? n_items : claim();
+        int kvc = 0;
+        for (int n = 0;; ++n) {
+          int item = -1;
+          Item it;
+          while (pending < n_items) {
+            const int c = pending;
+            pending = claim();
+            if (decode(c, it)) { item = c; break; }
+          }
+          const int slot = n % NI;
+          if (n >= NI && !mbar_wait(item_empty + slot, ((n / NI) - 1) & 1, p.err, kErrAttnProducer)) break;
+          item_slot[slot] = item;
+          mbar_arrive(item_full + slot);
+          if (item < 0) break;
+          const int qb = n & 1;
+          if (n >= 2 && !mbar_wait(q_empty + qb, ((n >> 1) - 1) & 1, p.err, kErrAttnProducer)) break;
+          mbar_expect_tx(q_full + qb, (it.has1 ? 2 : 1) * Cfg::kTile);
+          for (int t = 0; t < (it.has1 ? 2 : 1); ++t)
 #pragma unroll
-          for (int a = 0; a < Cfg::kAtoms; ++a)
-            tma_load_2d(sQ + (qb * 2 + t) * Cfg::kTile + a * Cfg::kAtomBytes, &tmQ, q_full + qb,
-                        a * Cfg::kAtomCols, it.bh * p.S + (it.q0 + t) * 128);
+            for (int a = 0; a < Cfg::kAtoms; ++a)
+              tma_load_2d(sQ + (qb * 2 + t) * Cfg::kTile + a * Cfg::kAtomBytes, &tmQ, q_full + qb,
+                          a * Cfg::kAtomCols, it.bh * p.S + (it.q0 + t) * 128);
+          bool ok = true;
+          for (int j = 0; j < it.n_kv; ++j) {
+            const int g = kvc + j, st = g % ST;
+            if (!mbar_wait(kv_empty + st, ((g / ST) & 1) ^ 1, p.err, kErrAttnProducer)) { ok = false; break; }
+            uint8_t* sk = sKV + st * 2 * Cfg::kTile;
+            mbar_expect_tx(kv_full + st, 2 * Cfg::kTile);
+#pragma unroll
+            for (int a = 0; a < Cfg::kAtoms; ++a) {
+              tma_load_2d(sk + a * Cfg::kAtomBytes, &tmK, kv_full + st, a * Cfg::kAtomCols, kv_row(it, j));
+              tma_load_2d(sk + Cfg::kTile + a * Cfg::kAtomBytes, &tmV, kv_full + st, a * Cfg::kAtomCols,
+                          kv_row(it, j));
+            }
+          }
+          if (!ok) break;
+          kvc += it.n_kv;
+        }
+      }
+    } else if (warp == 9) {
+      // ------------------------------------------------------------ S issuer (whole warp, elected lane issues)
+      constexpr uint32_t idesc_qk = idesc_f16_f32(128, 128, false, false);
+      int kvc = 0;
+      int cs[2] = {0, 0};  // S_t computed so far
+      bool ok = true;
+      for (int n = 0; ok; ++n) {
+        int item;
+        if (!next_item(n, item, kErrAttnMma) || item < 0) break;
+        Item it;
+        decode(item, it);
+        const int qb = n & 1;
+        if (!mbar_wait_warp(q_full + qb, (n >> 1) & 1, p.err, kErrAttnMma)) break;
+        const uint32_t q_addr = smem_u32(sQ + qb * 2 * Cfg::kTile);
+        for (int j = 0; j < it.n_kv && ok; ++j) {
+          const int g = kvc + j, st = g % ST;
+          if (!mbar_wait_warp(kv_full + st, (g / ST) & 1, p.err, kErrAttnMma)) { ok = false; break; }
+          const uint32_t k_addr = smem_u32(sKV + st * 2 * Cfg::kTile);
+#pragma unroll
+          for (int t = 0; t < 2; ++t) {
+            if (j >= (t == 0 ? it.nkv0 : it.nkv1)) continue;
+            // S_t is free once the softmax has read the previous S_t
+            if (cs[t] > 0 && !mbar_wait_warp(s_free + t, (cs[t] - 1) & 1, p.err, kErrAttnMma)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t qa = q_addr + t * Cfg::kTile;
+#pragma unroll
+            for (int ks = 0; ks < HD / 16; ++ks) {
+              const int atom = (ks * 16) / Cfg::kAtomCols;
+              const int within = ((ks * 16) % Cfg::kAtomCols) * 2;
+              const uint64_t ad = smem_desc(qa + atom * Cfg::kAtomBytes + within, 16, 8 * Cfg::kRowB, Cfg::kSw);
+              const uint64_t bd = smem_desc(k_addr + atom * Cfg::kAtomBytes + within, 16, 8 * Cfg::kRowB, Cfg::kSw);
+              umma_f16_ss_elect(tmem + Cfg::kColS + t * 128, ad, bd, idesc_qk, ks != 0);
+            }
+            umma_commit_elect(s_full + t);
+            ++cs[t];
+          }
+          if (!ok) break;
+          umma_commit_elect(kv_empty + st);  // K_j read once this warp's S MMAs retire
+        }
+        if (!ok) break;
+        umma_commit_elect(q_empty + qb);  // both Q tiles read
+        kvc += it.n_kv;
+      }
+    } else {
+      // ------------------------------------------------------------ P.V issuer of query tile t
+      constexpr uint32_t idesc_pv = idesc_f16_f32(128, HD, false, true);
+      const int t = warp - 10;
+      const uint32_t o_tmem = tmem + Cfg::kColO + t * HD;
+      const uint32_t p_tmem = tmem + Cfg::kColP + t * 64;
+      int kvc = 0, cp = 0;  // cp: P_t consumed so far
+      bool ok = true;
+      for (int n = 0; ok; ++n) {
+        int item;
+        if (!next_item(n, item, kErrAttnMma) || item < 0) break;
+        Item it;
+        decode(item, it);
+        const int nkv_t = t == 0 ? it.nkv0 : it.nkv1;
         for (int j = 0; j < it.n_kv; ++j) {
           const int g = kvc + j, st = g % ST;
-          if (!mbar_wait(kv_empty + st, ((g / ST) & 1) ^ 1, p.err, kErrAttnProducer)) { ok = false; break; }
-          uint8_t* sk = sKV + st * 2 * Cfg::kTile;
-          mbar_expect_tx(kv_full + st, 2 * Cfg::kTile);
-#pragma unroll
-          for (int a = 0; a < Cfg::kAtoms; ++a) {
-            tma_load_2d(sk + a * Cfg::kAtomBytes, &tmK, kv_full + st, a * Cfg::kAtomCols, kv_row(it, j));
-            tma_load_2d(sk + Cfg::kTile + a * Cfg::kAtomBytes, &tmV, kv_full + st, a * Cfg::kAtomCols,
-                        kv_row(it, j));
-          }
-        }
-        kvc += it.n_kv;
-        ++nitem;
-      }
-    }
-  } else if (warp == 9 || warp == 10) {
-    {  // the whole warp: every wait agrees in all lanes; tcgen05 issues come from the elected lane
-      // ---------------------------------------------------------- MMA issuers
-      // Warp 9 issues query tile 0's S and PV, warp 10 tile 1's, each over the
-      // same item sequence; both release every K/V stage and Q buffer (count
-      // 2), by a commit after their MMAs or, where their tile takes no part,
-      // by a plain arrive once the stage or buffer has landed.
-      constexpr uint32_t idesc_qk = idesc_f16_f32(128, 128, false, false);
-      constexpr uint32_t idesc_pv = idesc_f16_f32(128, HD, false, true);
-      const int t = warp - 9;
-      int kvc = 0, nitem = 0;
-      int cs = 0;  // S_t computed so far
-      int ci = 0;  // items in which tile t took part so far
-      bool ok = true;
-      for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x) {
-        Item it;
-        if (!decode(i, it)) continue;
-        const int qb = nitem & 1;
-        const int nkv_t = t == 0 ? it.nkv0 : it.nkv1;
-        if (!mbar_wait_warp(q_full + qb, (nitem >> 1) & 1, p.err, kErrAttnMma)) break;
-        const uint32_t q_addr = smem_u32(sQ + qb * 2 * Cfg::kTile) + t * Cfg::kTile;
-        auto kv_addr = [&](int j) { return smem_u32(sKV + ((kvc + j) % ST) * 2 * Cfg::kTile); };
-        auto issue_s = [&](uint32_t k_addr) {
-#pragma unroll
-          for (int ks = 0; ks < HD / 16; ++ks) {
-            const int atom = (ks * 16) / Cfg::kAtomCols;
-            const int within = ((ks * 16) % Cfg::kAtomCols) * 2;
-            const uint64_t ad = smem_desc(q_addr + atom * Cfg::kAtomBytes + within, 16, 8 * Cfg::kRowB, Cfg::kSw);
-            const uint64_t bd = smem_desc(k_addr + atom * Cfg::kAtomBytes + within, 16, 8 * Cfg::kRowB, Cfg::kSw);
-            umma_f16_ss_elect(tmem + Cfg::kColS + t * 128, ad, bd, idesc_qk, ks != 0);
-          }
-          umma_commit_elect(s_full + t);
-        };
-        for (int j = 0; j < it.n_kv && ok; ++j) {
-          const int g = kvc + j;
-          if (!mbar_wait_warp(kv_full + g % ST, (g / ST) & 1, p.err, kErrAttnMma)) { ok = false; break; }
-          tc_fence_after();
-          if (j >= nkv_t) {
-            mbar_arrive_elect(kv_empty + g % ST);
+          if (!mbar_wait_warp(kv_full + st, (g / ST) & 1, p.err, kErrAttnMma)) { ok = false; break; }
+          if (j >= nkv_t) {  // this tile is done with the item: release the stage as it lands
+            mbar_arrive_elect(kv_empty + st);
             continue;
           }
-          if (j == 0) {  // S_t(0) once the previous item's last S_t has been read
-            if (cs > 0 && !mbar_wait_warp(s_free + t, (cs - 1) & 1, p.err, kErrAttnMma)) { ok = false; break; }
-            tc_fence_after();
-            issue_s(kv_addr(0));
-          }
-          if (j + 1 < nkv_t) {
-            const int gn = g + 1;
-            if (!mbar_wait_warp(kv_full + gn % ST, (gn / ST) & 1, p.err, kErrAttnMma)) { ok = false; break; }
-            if (!mbar_wait_warp(s_free + t, (cs + j) & 1, p.err, kErrAttnMma)) { ok = false; break; }
-            tc_fence_after();
-            issue_s(kv_addr(j + 1));
-          }
-          if (!mbar_wait_warp(p_full + t, (cs + j) & 1, p.err, kErrAttnMma)) { ok = false; break; }
-          if (j == 0 && ci > 0 && !mbar_wait_warp(o_free + t, (ci - 1) & 1, p.err, kErrAttnMma)) { ok = false; break; }
+          if (!mbar_wait_warp(p_full + t, cp & 1, p.err, kErrAttnMma)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t o_tmem = tmem + Cfg::kColO + t * HD;
-          const uint32_t p_tmem = tmem + Cfg::kColP + t * 64;
-          const uint32_t v_addr = kv_addr(j) + Cfg::kTile;
+          const uint32_t v_addr = smem_u32(sKV + st * 2 * Cfg::kTile) + Cfg::kTile;
 #pragma unroll
           for (int ks = 0; ks < 8; ++ks) {
             const uint64_t bd = smem_desc(v_addr + ks * 16 * Cfg::kRowB, Cfg::kAtomBytes, 8 * Cfg::kRowB, Cfg::kSw);
@@ -578,19 +653,15 @@ __global__ void __launch_bounds__(AttnCfg<HD>::kThreadsPersist, 1)
           }
           umma_commit_elect(pv_done + t);
           if (j == nkv_t - 1) umma_commit_elect(o_final + t);
-          umma_commit_elect(kv_empty + g % ST);
+          umma_commit_elect(kv_empty + st);
+          ++cp;
         }
-        if (!ok) break;
-        if (nkv_t > 0) umma_commit_elect(q_empty + qb);  // after this tile's S MMAs read Q
-        else mbar_arrive_elect(q_empty + qb);
         kvc += it.n_kv;
-        cs += nkv_t;
-        ci += nkv_t > 0 ? 1 : 0;
-        ++nitem;
       }
     }
   } else {
-    // ------------------------------------------------------------ softmax + epilogue
+    reg_alloc<PC::kRegSoftmax>();
+    // -------------------------------------------------------------- softmax + epilogue
     const int t = warp >> 2;
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;
@@ -599,19 +670,45 @@ __global__ void __launch_bounds__(AttnCfg<HD>::kThreadsPersist, 1)
     const uint32_t p_col = tmem + lane_off + Cfg::kColP + t * 64;
     const uint32_t o_col = tmem + lane_off + Cfg::kColO + t * HD;
     const float sl2 = p.scale_log2;
-    int cs = 0, ci = 0;
+    // Normalise this thread's O row and store it as the fp16 context row.
+    auto store_o = [&](__half* dst, float inv) {
+#pragma unroll
+      for (int c = 0; c < HD / 32; ++c) {
+        uint32_t o[32];
+        tmem_ld32(o_col + c * 32, o);
+        tmem_ld_wait();
+        if (dst != nullptr) {
+#pragma unroll
+          for (int i2 = 0; i2 < 32; i2 += 8) {
+            uint4 w;
+            w.x = pack_half2(__uint_as_float(o[i2]) * inv, __uint_as_float(o[i2 + 1]) * inv);
+            w.y = pack_half2(__uint_as_float(o[i2 + 2]) * inv, __uint_as_float(o[i2 + 3]) * inv);
+            w.z = pack_half2(__uint_as_float(o[i2 + 4]) * inv, __uint_as_float(o[i2 + 5]) * inv);
+            w.w = pack_half2(__uint_as_float(o[i2 + 6]) * inv, __uint_as_float(o[i2 + 7]) * inv);
+            *reinterpret_cast<uint4*>(dst + c * 32 + i2) = w;
+          }
+        }
+      }
+    };
+    int cs = 0;  // S_t / P_t uses so far
+    int co = 0;  // items of this tile drained so far
+    bool pending = false;  // an item's O_t still waits in TMEM
+    __half* prev_dst = nullptr;
+    float prev_inv = 0.0f;
     bool ok = true;
-    for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x) {
+    for (int n = 0; ok; ++n) {
+      int item;
+      if (!next_item(n, item, kErrAttnSoftmax)) { ok = false; break; }
+      if (item < 0) break;
       Item it;
-      if (!decode(i, it)) continue;
+      decode(item, it);
       const int nkv_t = t == 0 ? it.nkv0 : it.nkv1;
       if (nkv_t == 0) continue;
-      const int qt = it.q0 + t;
-      const int qrow = qt * 128 + r;
+      const int qrow = (it.q0 + t) * 128 + r;
       const uint8_t* kmask = it.general ? p.mask + (size_t)it.b * p.S : nullptr;
       float m_run = -INFINITY, l_run = 0.0f;
       for (int j = 0; j < nkv_t; ++j) {
-        const int u = cs + j;  // global use index of S_t / P_t
+        const int u = cs + j;
         if (!mbar_wait(s_full + t, u & 1, p.err, kErrAttnSoftmax)) { ok = false; break; }
         tc_fence_after();
         uint32_t s[128];
@@ -621,7 +718,7 @@ __global__ void __launch_bounds__(AttnCfg<HD>::kThreadsPersist, 1)
         tmem_ld32(s_col + 96, *reinterpret_cast<uint32_t(*)[32]>(s + 96));
         tmem_ld_wait();
         tc_fence_before();
-        mbar_arrive(s_free + t);
+        mbar_arrive(s_free + t);  // S_t may now be overwritten
         const int kbase = j * 128;
         const bool diag = p.causal && j == it.qg0 + t;
         const bool tail = kbase + 128 > it.len;
@@ -636,14 +733,25 @@ __global__ void __launch_bounds__(AttnCfg<HD>::kThreadsPersist, 1)
         const bool grow = m_tile > m_run + Cfg::kRescaleLog2;
         float alpha = 1.0f;
         if (grow) {
-          alpha = fast_exp2(m_run - m_tile);
+          alpha = fast_exp2(m_run - m_tile);  // 0 when m_run = -inf
           m_run = m_tile;
         }
         const float msub = m_run == -INFINITY ? 0.0f : m_run;
         const float rowsum = exp_pack_rowsum(s, sl2, msub);
-        // P_t and O_t are free once the previous PV_t (this item's or the last item's) retired
-        if (u > 0 && !mbar_wait(pv_done + t, (u - 1) & 1, p.err, kErrAttnSoftmax)) { ok = false; break; }
-        tc_fence_after();
+        if (j == 0) {
+          if (pending) {
+            // the previous item's last P.V has retired: P_t is free and its O_t final
+            if (!mbar_wait(o_final + t, co & 1, p.err, kErrAttnSoftmax)) { ok = false; break; }
+            tc_fence_after();
+            store_o(prev_dst, prev_inv);
+            ++co;
+            pending = false;
+          }
+        } else {
+          // P_t and O_t are free once P.V_t(j-1) has retired
+          if (!mbar_wait(pv_done + t, (u - 1) & 1, p.err, kErrAttnSoftmax)) { ok = false; break; }
+          tc_fence_after();
+        }
         tmem_st32(p_col, *reinterpret_cast<uint32_t(*)[32]>(s));
         tmem_st32(p_col + 32, *reinterpret_cast<uint32_t(*)[32]>(s + 32));
         l_run = l_run * alpha + rowsum;
@@ -663,38 +771,29 @@ __global__ void __launch_bounds__(AttnCfg<HD>::kThreadsPersist, 1)
         mbar_arrive(p_full + t);
       }
       if (!ok) break;
-      if (!mbar_wait(o_final + t, ci & 1, p.err, kErrAttnSoftmax)) { ok = false; break; }
-      tc_fence_after();
-      const float inv = l_run > 0.0f ? 1.0f / l_run : 0.0f;
-      __half* dst = p.ctx + ((size_t)it.b * p.S + qrow) * p.d_model + (size_t)it.h * HD;
-      const bool store = qrow < p.S;
-#pragma unroll
-      for (int c = 0; c < HD / 32; ++c) {
-        uint32_t o[32];
-        tmem_ld32(o_col + c * 32, o);
-        tmem_ld_wait();
-        if (store) {
-#pragma unroll
-          for (int i2 = 0; i2 < 32; i2 += 8) {
-            uint4 w;
-            w.x = pack_half2(__uint_as_float(o[i2]) * inv, __uint_as_float(o[i2 + 1]) * inv);
-            w.y = pack_half2(__uint_as_float(o[i2 + 2]) * inv, __uint_as_float(o[i2 + 3]) * inv);
-            w.z = pack_half2(__uint_as_float(o[i2 + 4]) * inv, __uint_as_float(o[i2 + 5]) * inv);
-            w.w = pack_half2(__uint_as_float(o[i2 + 6]) * inv, __uint_as_float(o[i2 + 7]) * inv);
-            *reinterpret_cast<uint4*>(dst + c * 32 + i2) = w;
-          }
-        }
-      }
-      tc_fence_before();
-      mbar_arrive(o_free + t);  // O_t may be overwritten by the next item
       cs += nkv_t;
-      ++ci;
+      pending = true;
+      prev_inv = l_run > 0.0f ? 1.0f / l_run : 0.0f;
+      prev_dst = qrow < p.S ? p.ctx + ((size_t)it.b * p.S + qrow) * p.d_model + (size_t)it.h * HD : nullptr;
+    }
+    if (ok && pending && mbar_wait(o_final + t, co & 1, p.err, kErrAttnSoftmax)) {
+      tc_fence_after();
+      store_o(prev_dst, prev_inv);
     }
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   if (warp == 9) tmem_dealloc(tmem, Cfg::kTmemCols);
+  if (threadIdx.x == 0 && p.sched != nullptr) {
+    // the last CTA out resets the scheduler for the next launch (every CTA's
+    // producer has stopped claiming by the time it counts itself done)
+    __threadfence();
+    if (atomicAdd(p.sched + 1, 1) == (int)gridDim.x - 1) {
+      atomicExch(p.sched, 0);
+      atomicExch(p.sched + 1, 0);
+    }
+  }
 }
 
 }  // namespace tj

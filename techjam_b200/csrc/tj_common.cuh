@@ -1,10 +1,11 @@
 // Shared device helpers for the sm_100a kernels: mbarriers with bounded waits,
 // TMA tile loads, tcgen05 (UMMA) descriptors / MMA / TMEM access.
 //
-// Every spin-wait is bounded: after TJ_WAIT_NS of wall time (globaltimer) the
-// waiting thread records a site code in the device error word and returns
-// false; the kernel then unwinds (releasing TMEM) instead of hanging the GPU.
-// Any CTA that finds the error word already set bails out at its next wait.
+// Every spin-wait is bounded: after g_tj_wait_ns of wall time (globaltimer,
+// TJ_WAIT_NS unless the host set another limit) the waiting thread records a
+// site code in the device error word and returns false; the kernel then
+// unwinds (releasing TMEM) instead of hanging the GPU.  Any CTA that finds the
+// error word already set bails out at its next wait.
 #pragma once
 #include <cuda.h>
 #include <cuda_fp16.h>
@@ -19,13 +20,17 @@
 
 namespace tj {
 
+// Limit of every bounded wait on this device, in ns of globaltimer time
+// (tj_set_wait_limit); read once by each wait that does not succeed at once.
+__device__ unsigned long long g_tj_wait_ns = TJ_WAIT_NS;
+
 // Error-site codes written to the device error word (first writer wins).
 enum ErrSite : int {
   kErrNone = 0,
   kErrGemmProducer = 101, kErrGemmMma = 102, kErrGemmEpilogue = 103,
   kErrAttnProducer = 201, kErrAttnMma = 202, kErrAttnSoftmax = 203,
   kErrPolyWait = 301,
-  kErrTest = 900,
+  kErrTest = 900,  // tj_wait_selftest: a wait that nothing completes
 };
 
 TJ_DEV uint32_t smem_u32(const void* p) {
@@ -65,11 +70,12 @@ TJ_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 TJ_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int site) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_ns();
+  const uint64_t limit = *reinterpret_cast<volatile unsigned long long*>(&g_tj_wait_ns);
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 63u) == 0) {
       if (*reinterpret_cast<volatile int*>(err) != 0) return false;
-      if (global_ns() - t0 > TJ_WAIT_NS) {
+      if (global_ns() - t0 > limit) {
         atomicCAS(err, 0, site);
         return false;
       }
@@ -118,6 +124,19 @@ TJ_DEV void tmem_dealloc(uint32_t taddr, uint32_t ncols) {  // whole warp
 }
 TJ_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 TJ_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Per-warpgroup register budget (every warp of a warpgroup executes the same
+// one).  An increase waits until other warpgroups have released enough of the
+// registers the CTA was launched with, so the budgets must add up to exactly
+// that launch total (launchers check the kernel's register count).
+template <int N>
+TJ_DEV void reg_alloc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+TJ_DEV void reg_dealloc() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
 
 // tcgen05 issues, made by the elected lane of a converged warp (elect.sync
 // picks the same lane every time while all 32 lanes are active, so a commit

@@ -9,10 +9,13 @@ constexpr int kTileRows = 128;
 
 // Per sample: length = 1 + last valid position (0 if none); general = mask is
 // not a right-padded prefix.  mask == null means every position is valid.
+// sched (nullable): the attention scheduler's two words, zeroed here so that a
+// forward starts from a clean scheduler even after an aborted launch.
 __global__ void __launch_bounds__(1024) prep_lengths_kernel(const uint8_t* __restrict__ mask, int S,
                                                              int* __restrict__ lengths,
-                                                             uint8_t* __restrict__ general) {
+                                                             uint8_t* __restrict__ general, int* __restrict__ sched) {
   const int b = blockIdx.x;
+  if (sched != nullptr && b == 0 && threadIdx.x < 2) sched[threadIdx.x] = 0;
   if (mask == nullptr) {
     if (threadIdx.x == 0) { lengths[b] = S; general[b] = 0; }
     return;
@@ -189,6 +192,20 @@ __global__ void __launch_bounds__(256) layernorm_kernel(const float* __restrict_
       }
     }
   }
+}
+
+// Failure-path self-test: one warp waits, through the same bounded wait every
+// kernel uses, on an mbarrier that nothing arrives at.  The wait runs out
+// after the device's wait limit, records kErrTest in *err and the kernel
+// returns -- no fault, trap or hang, and the context stays usable.
+__global__ void wait_selftest_kernel(int* err) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncwarp();
+  mbar_wait_warp(&bar, 0, err, kErrTest);
 }
 
 // dst = fp16(src), element-wise, for the packed weight buffers.

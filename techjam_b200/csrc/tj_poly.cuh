@@ -53,6 +53,7 @@ struct PolyCtl {
   float sigma;
   float max_abs;
   double sum, sumsq, maxv;  // guard accumulators
+  int sched[2];             // work scheduler of the exact-prefix flash launch
 };
 
 struct PolyParams {

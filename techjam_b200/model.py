@@ -254,3 +254,11 @@ class B200Transformer(nn.Module):
             _lib.call("tj_device_error", self._handle.ptr, ctypes.byref(code))
         return int(code.value)
 
+    def check_device(self) -> None:
+        """Raise ``TjError`` (status TJ_ERR_DEVICE) if a kernel's bounded wait
+        expired since the last check; the word is cleared either way."""
+        code = self.device_error()
+        if code != 0:
+            raise _lib.TjError(_lib.TJ_ERR_DEVICE, f"a kernel's bounded wait expired (site {code}); "
+                               "its outputs are incomplete")
+

@@ -111,18 +111,25 @@ def gemm(a: torch.Tensor, w: torch.Tensor, bias: torch.Tensor, info: MaskInfo, e
 
 
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, info: MaskInfo, causal: bool,
-              err: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """Flash attention over fp16 [B, H, N, hd]; returns the fp16 context [B*N, H*hd]."""
+              err: Optional[torch.Tensor] = None, sched: Optional[torch.Tensor] = None,
+              dynamic: bool = True) -> torch.Tensor:
+    """Flash attention over fp16 [B, H, N, hd]; returns the fp16 context [B*N, H*hd].
+
+    ``sched``: two zeroed int32 words for the dynamic work scheduler (made
+    here when not given); ``dynamic=False`` uses the static item assignment.
+    """
     _need_cuda(q, k, v)
     b, h, n, hd = q.shape
     if q.dtype != torch.float16 or k.shape != q.shape or v.shape != q.shape:
         raise ValueError("q, k, v must be fp16 [B, H, N, hd]")
     err = err if err is not None else torch.zeros(1, dtype=torch.int32, device=q.device)
+    if dynamic and sched is None:
+        sched = torch.zeros(2, dtype=torch.int32, device=q.device)
     ctx = torch.zeros(b * n, h * hd, dtype=torch.float16, device=q.device)
     with torch.cuda.device(q.device):
         _lib.call("tj_attention_f16", q.data_ptr(), k.data_ptr(), v.data_ptr(), ctx.data_ptr(), b, h, n, hd,
                   int(causal), info.lengths.data_ptr(), _ptr(info.mask), info.general.data_ptr(), err.data_ptr(),
-                  _stream(q))
+                  _ptr(sched) if dynamic else None, _stream(q))
     return ctx
 
 

@@ -158,3 +158,27 @@ def test_attention_matches_fp32(b, h, n, hd, causal, kind):
     ref = _attn_ref(q, k, v, mask, causal)
     rows_ok = mask.reshape(-1)
     torch.testing.assert_close(got[rows_ok], ref[rows_ok], atol=4e-3, rtol=1e-2)
+
+
+@pytest.mark.parametrize("b,h,n,hd,causal", [(4, 8, 2048, 64, True), (16, 4, 256, 64, True), (3, 4, 1500, 32, True),
+                                             (2, 4, 1100, 64, False)])
+def test_attention_scheduler_static_equals_dynamic(b, h, n, hd, causal):
+    """The persistent kernel's work items are independent: claiming them
+    through the atomic scheduler or by static round-robin gives bit-identical
+    contexts, and the scheduler words are zero again after every launch."""
+    gen = torch.Generator().manual_seed(b * 31 + n)
+    q, k, v = (torch.randn(b, h, n, hd, generator=gen).half().to(DEV) for _ in range(3))
+    mask = _right_padded(b, n, n // 2, gen)
+    info = ops.prepare_mask(mask.to(DEV), b, n)
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    sched = torch.zeros(2, dtype=torch.int32, device=DEV)
+    dyn = [ops.attention(q, k, v, info, causal, err=err, sched=sched) for _ in range(3)]
+    torch.cuda.synchronize()
+    assert sched.tolist() == [0, 0]
+    static = ops.attention(q, k, v, info, causal, err=err, dynamic=False)
+    assert int(err.item()) == 0
+    for d in dyn:
+        assert torch.equal(d, static)
+    ref = _attn_ref(q.cpu(), k.cpu(), v.cpu(), mask, causal)
+    rows_ok = mask.reshape(-1)
+    torch.testing.assert_close(static.float().cpu()[rows_ok], ref[rows_ok], atol=4e-3, rtol=1e-2)
