@@ -11,15 +11,19 @@ fixed: ``scaling: strong``; ``value`` is the max-over-ranks latency.
 
 One JSON line on rank 0.  ``value`` = device-timed forward latency (inputs
 resident in HBM, CUDA events on the launching stream, barrier + synchronize
-on both sides).  ``e2e`` = the same forward through the public API
-(``DispatchingTransformer.forward``) including the host->device copy of x and
-the mask from pinned memory and the device->host copy of the output.
-``roofline`` = the dominant kernel class measured live with per-launch CUDA
-events (libtj's profiler) in a second pass over the same inputs.
+on both sides; for N > 1 including the gather of every rank's output rows
+into rank 0's [B, N, d] buffer, ``value_no_gather`` without it).  ``e2e`` =
+the latency of one call through the public API
+(``DispatchingTransformer.forward``) with the host->device copy of x and the
+mask from pinned memory and the device->host copy of the output inside the
+timed region; ``e2e.pipelined_ms`` = the per-step time when consecutive
+calls overlap their copies.  ``roofline`` = the dominant kernel class,
+measured live with per-launch CUDA events (libtj's profiler) in a second
+pass over the same inputs, against the measured burst peak.
 ``cpu_baseline`` = the oracle (an FP32 restatement of the reference dense
-model) on the host cores for one sample, extrapolated to the batch by
-algorithmic work.  ``--impl reference`` times that same CPU model as the
-reference arm.
+model) on all host cores for whole batches of the workload.  ``--impl
+reference`` times that same CPU model as the reference arm, one full batch
+per step.
 """
 
 from __future__ import annotations
@@ -45,19 +49,22 @@ sys.path.insert(0, str(ROOT))
 from techjam_b200 import _lib  # noqa: E402
 from techjam_b200.dispatcher import DispatchingTransformer  # noqa: E402
 from techjam_b200.harness import CONFIGS, generate_random_case, seeded_model, valid_lengths, work  # noqa: E402
-from techjam_b200.sharding import SeqShardComm, forward_seqshard, shard_samples, token_range  # noqa: E402
+from techjam_b200.sharding import (SeqShardComm, forward_seqshard, gather_batch_outputs, sample_owners,  # noqa: E402
+                                   shard_samples, token_range)
 
 SEED = 1234 + 100000  # the reference harness's timing input seed (torch_transformer_benchmark.py:459-466)
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 # dram__bytes_read.sum + dram__bytes_write.sum of one launch of the workload's dominant
-# kernel, from ncu captures of this build (profiles/*.md), keyed (workload, kernel class).
+# kernel, from the ncu captures summarised in profiles/, keyed (workload, kernel class).
 NCU_TRAFFIC_BYTES: dict = {
-    ("C1", "attention"): 2632192 + 0,               # attn_fwd_persistent_kernel<32>
-    ("C2", "attention"): 141863424 + 32032768,      # attn_fwd_kernel<64>
+    ("C2", "attention"): 205816320 + 24682752,      # attn_fwd_persistent_kernel<64>
+    ("C2", "gemm_ffn_in"): 55705600 + 140115968,    # gemm_tc2_kernel<1>
     ("C3", "gemm_ffn_in"): 57665792 + 168056064,    # gemm_tc_kernel<256,1>
-    ("C4", "attention"): 1780000000 + 576210000,    # attn_fwd_kernel<64>
 }
 CPU_DENSE_MAX = 8192  # longest sample the CPU baseline runs through the dense model
+# Whole batches whose dense [B, H, N, N] FP32 scores fit comfortably in host memory
+# run as one call; larger ones (C4, C5) run per sample and scale by algorithmic work.
+CPU_FULL_BATCH_SCORE_BYTES = 8e9
 
 
 def parse_args():
@@ -154,10 +161,38 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------ CPU baseline (oracle)
+def full_batch_on_cpu(cfg) -> bool:
+    """Does the dense reference model run the whole batch as one CPU call?"""
+    return 4.0 * cfg.batch_size * cfg.num_heads * cfg.seq_len ** 2 <= CPU_FULL_BATCH_SCORE_BYTES
+
+
+def cpu_full_batch_ms(cfg, wl, x_full, mask_full, steps, warmup):
+    """Time the oracle (FP32 restatement of the reference dense model) on every
+    host core, one whole-batch forward per step, as the reference's
+    ``benchmark_once`` times one call (torch_transformer_benchmark.py:501-506).
+    Returns the per-step times (ms) and the thread count."""
+    from oracle.reference_model import OracleEncoder  # CPU-baseline / reference-arm leg only
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    model = seeded_model(OracleEncoder, cfg, 1234, wl.linear_scale)
+    x, m = x_full.cpu(), mask_full.cpu()
+    times = []
+    with torch.inference_mode():
+        for s in range(warmup + steps):
+            t0 = time.perf_counter_ns()
+            model(x, m)
+            t1 = time.perf_counter_ns()
+            if s >= warmup:
+                times.append((t1 - t0) / 1e6)
+    return times, threads
+
+
 def cpu_reference_ms(cfg, wl, x_full, mask_full, lengths, steps, warmup, sample_index=None):
     """Time the oracle (FP32 restatement of the reference dense model) on the host
     CPU for single samples; return full-batch-equivalent ms per step (scaled by
-    algorithmic work), the thread count and a sample description."""
+    algorithmic work), the thread count and a sample description.  Used where
+    the whole batch's dense scores do not fit in host memory (C4, C5)."""
     from oracle.linear_memory import linear_memory_forward  # CPU-baseline leg only
     from oracle.reference_model import OracleEncoder
 
@@ -197,7 +232,18 @@ def run_reference(args):
     cfg = wl.config
     x, mask = generate_random_case(cfg, torch.device("cpu"), torch.float32, SEED, wl.padding_ratio)
     lengths = valid_lengths(mask, cfg.batch_size, cfg.seq_len)
-    ms, threads, idx, prefix = cpu_reference_ms(cfg, wl, x, mask, lengths, args.steps, args.warmup)
+    if full_batch_on_cpu(cfg):
+        times, threads = cpu_full_batch_ms(cfg, wl, x, mask, args.steps, args.warmup)
+        ms = statistics.mean(times)
+        sample = (f"the whole batch (B={cfg.batch_size}) through the oracle FP32 dense model, one call per step, "
+                  f"on {threads} host threads; no extrapolation")
+    else:
+        ms, threads, idx, prefix = cpu_reference_ms(cfg, wl, x, mask, lengths, args.steps, args.warmup)
+        sample = (f"one B=1 sample per step (cycling samples 0..{cfg.batch_size - 1}"
+                  + (f", first {prefix} tokens, bounded-memory oracle" if prefix < cfg.seq_len
+                     else ", oracle FP32 dense model")
+                  + ") on host CPU, scaled to the full batch by algorithmic flops (the batch's dense scores do "
+                  "not fit in host memory)")
     line = {
         "impl": "reference", "metric": "fwd_latency_ms", "value": round(ms, 3), "unit": "ms", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": False,
@@ -205,11 +251,7 @@ def run_reference(args):
         "config": {"workload": wl.name, "batch": cfg.batch_size, "seq_len": cfg.seq_len, "d_model": cfg.d_model,
                    "heads": cfg.num_heads, "ffn_dim": cfg.ffn_dim, "layers": cfg.num_layers,
                    "padding_ratio": wl.padding_ratio},
-        "cpu_baseline": {"value": round(ms, 3), "unit": "ms", "cores": threads, "kind": "port",
-                         "sample": (f"one B=1 sample per step (cycling samples 0..{cfg.batch_size - 1}"
-                                    + (f", first {prefix} tokens, bounded-memory oracle" if prefix < cfg.seq_len
-                                       else ", oracle FP32 dense model")
-                                    + ") on host CPU, scaled to the full batch by algorithmic flops")},
+        "cpu_baseline": {"value": round(ms, 3), "unit": "ms", "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": round(ms, 3), "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -392,6 +434,9 @@ def main():
         def fwd(inp, msk):
             return forward_seqshard(model, comm, inp, args.route)
     else:
+        if cfg.batch_size < world:
+            raise SystemExit(f"{wl.name} has {cfg.batch_size} samples: batch sharding needs at least one per GPU "
+                             f"({world} GPUs)")
         mine = shard_samples(lengths, world, rank, cfg.d_model, cfg.ffn_dim)
         sel = torch.tensor(mine, device=dev, dtype=torch.long)
         x = x_full.index_select(0, sel).contiguous()
@@ -405,6 +450,17 @@ def main():
         def fwd(inp, msk):
             return model(inp, msk)
 
+    # batch sharding: every rank's output rows land in rank 0's [B, N, d] buffer
+    owners = sample_owners(lengths, world, cfg.d_model, cfg.ffn_dim) if (world > 1 and not seqshard) else None
+    out_full = (torch.empty(cfg.batch_size, cfg.seq_len, cfg.d_model, dtype=torch.float32, device=dev)
+                if owners is not None and rank == 0 else None)
+
+    def step(inp, msk):
+        y = fwd(inp, msk)
+        if owners is not None:
+            gather_batch_outputs(y, owners, out_full)
+        return y
+
     def barrier():
         if world > 1:
             dist.barrier(device_ids=[local])
@@ -416,38 +472,45 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    with torch.inference_mode():
-        for _ in range(args.warmup):
-            fwd(x, mask)
-        torch.cuda.synchronize(dev)
-        if model.device_error() != 0:
-            raise RuntimeError("device error during warm-up")
-        # ---- timed region: K forwards, inputs resident in HBM
-        n0 = ctypes.c_longlong()
-        _lib.call("tj_launch_count", model._handle.ptr, ctypes.byref(n0))
-        g0 = model.graph_kernel_launches
+    def timed(fn):
+        """Device time of K calls of fn (barrier + synchronize on both sides), max over ranks."""
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         barrier()
         torch.cuda.synchronize(dev)
-        with ClockSampler(local) as clocks:
-            start.record(stream)
-            for _ in range(args.steps):
-                fwd(x, mask)
-            end.record(stream)
-            torch.cuda.synchronize(dev)
+        start.record(stream)
+        for _ in range(args.steps):
+            fn(x, mask)
+        end.record(stream)
+        torch.cuda.synchronize(dev)
         barrier()
-        ms_local = start.elapsed_time(end) / args.steps
+        return max_over_ranks(start.elapsed_time(end) / args.steps)
+
+    with torch.inference_mode():
+        for _ in range(args.warmup):
+            step(x, mask)
+        torch.cuda.synchronize(dev)
+        if model.device_error() != 0:
+            raise RuntimeError("device error during warm-up")
+        # ---- timed region: K forwards (+ the output gather when batch-sharded), inputs resident in HBM
+        n0 = ctypes.c_longlong()
+        _lib.call("tj_launch_count", model._handle.ptr, ctypes.byref(n0))
+        g0 = model.graph_kernel_launches
+        with ClockSampler(local) as clocks:
+            ms = timed(step)
         n1 = ctypes.c_longlong()
         _lib.call("tj_launch_count", model._handle.ptr, ctypes.byref(n1))
         launches = int(n1.value - n0.value) + (model.graph_kernel_launches - g0)
-        ms = max_over_ranks(ms_local)
+        ms_no_gather = timed(fwd) if owners is not None else ms
 
-        # ---- per-kernel pass (event pairs around every launch)
+        # ---- per-kernel pass (event pairs around every launch).  A spin kernel
+        # ahead of each forward lets the host enqueue the whole launch sequence
+        # before the GPU reaches it, so no event pair spans a host launch gap.
         per_fwd = 12 * cfg.num_layers + 4  # upper bound incl. the polynomial route's launches
         graphs_were = model.cuda_graphs
         model.cuda_graphs = False  # per-launch events need host launches
         _lib.call("tj_profile_begin", model._handle.ptr, per_fwd * args.steps)
         for _ in range(args.steps):
+            torch.cuda._sleep(4_000_000)  # ~2 ms of spinning at the B200's clocks
             fwd(x, mask)
         kms = (ctypes.c_double * 9)()
         kcnt = (ctypes.c_longlong * 9)()
@@ -460,17 +523,19 @@ def main():
         e2e = None
         if not args.no_e2e:
             serial_ms, piped_ms, h2d_b, d2h_b = end_to_end(fwd, x, mask, args.steps, args.warmup, stream, barrier)
-            e2e = {"value": round(max_over_ranks(piped_ms), 4), "unit": "ms",
+            e2e = {"value": round(max_over_ranks(serial_ms), 4), "unit": "ms",
                    "h2d_bytes_per_step": h2d_b, "d2h_bytes_per_step": d2h_b,
-                   "mode": ("pipelined: step i+1's host->device copy and step i-1's device->host copy run on "
-                            "their own streams under step i's forward (double-buffered pinned host and device "
-                            "staging)"),
-                   "serial_ms": round(max_over_ranks(serial_ms), 4)}
+                   "mode": ("latency of one call: copy-in from pinned host memory, forward, copy-out to pinned "
+                            "host memory, back to back on one stream"),
+                   "pipelined_ms": round(max_over_ranks(piped_ms), 4),
+                   "pipelined_mode": ("throughput per step when step i+1's host->device copy and step i-1's "
+                                      "device->host copy run on their own streams under step i's forward")}
 
     # aggregate per-kernel timing across ranks (max ms per class)
     kms_l = [max_over_ranks(kms[i] / args.steps) for i in range(9)]
     peaks, peak_src = load_peaks()
-    peak = peaks["bf16_tflops_sustained"]
+    # the kernels run for microseconds inside a few-millisecond step: burst figure
+    peak = peaks["bf16_tflops"]
     rates = kernel_rates(cfg, lengths, my_lengths, kms_l, list(kcnt), args.steps, world,
                          poly_prefix_here=(not seqshard or rank == 0))
     kernels, dom = rates["kernels"], rates["dominant"]
@@ -479,17 +544,26 @@ def main():
     traffic = NCU_TRAFFIC_BYTES.get((wl.name, dom))
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cms, threads, idx, prefix = cpu_reference_ms(cfg, wl, x_full, mask_full, lengths, args.cpu_repeats, 1,
-                                                     sample_index=0)
-        what = (f"first {prefix} tokens of sample 0, bounded-memory FP32 oracle" if prefix < cfg.seq_len
-                else f"sample 0 (B=1, {lengths[0]} valid tokens), oracle FP32 dense model")
-        cpu = {"value": round(cms, 1), "unit": "ms", "cores": threads, "kind": "port",
-               "sample": (f"{what} of the same workload on {threads} host threads, mean of {args.cpu_repeats} "
-                          "after 1 warm-up, scaled to the full batch by algorithmic flops")}
+        if full_batch_on_cpu(cfg):
+            times, threads = cpu_full_batch_ms(cfg, wl, x_full, mask_full, args.cpu_repeats, 1)
+            cpu = {"value": round(statistics.mean(times), 1), "unit": "ms", "cores": threads, "kind": "port",
+                   "sample": (f"the whole batch (B={cfg.batch_size}) of the same workload through the oracle FP32 "
+                              f"dense model on {threads} host threads, mean of {args.cpu_repeats} calls after 1 "
+                              "warm-up; no extrapolation")}
+        else:
+            cms, threads, idx, prefix = cpu_reference_ms(cfg, wl, x_full, mask_full, lengths, args.cpu_repeats, 1,
+                                                         sample_index=0)
+            what = (f"first {prefix} tokens of sample 0, bounded-memory FP32 oracle" if prefix < cfg.seq_len
+                    else f"sample 0 (B=1, {lengths[0]} valid tokens), oracle FP32 dense model")
+            cpu = {"value": round(cms, 1), "unit": "ms", "cores": threads, "kind": "port",
+                   "sample": (f"{what} of the same workload on {threads} host threads, mean of {args.cpu_repeats} "
+                              "after 1 warm-up, scaled to the full batch by algorithmic flops (the batch's dense "
+                              "scores do not fit in host memory)")}
 
     if rank == 0:
         line = {
-            "metric": "fwd_latency_ms", "value": round(ms, 4), "unit": "ms", "n_gpus": world, "steps": args.steps,
+            "metric": "fwd_latency_ms", "value": round(ms, 4), "value_no_gather": round(ms_no_gather, 4),
+            "unit": "ms", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": False, "scaling": "strong",
             "vs_baseline": None, "dtype": "f16 operands / f32 accumulate, f32 residual + interface",
             "data": "synthetic (reference generator, seed 101234; seeded default-init weights)",
@@ -498,6 +572,9 @@ def main():
                        "layers": cfg.num_layers, "causal": cfg.causal, "padding_ratio": wl.padding_ratio,
                        "linear_scale": wl.linear_scale, "route": args.route,
                        "parallelism": parallelism,
+                       "output": ("gathered into rank 0's [B, N, d] buffer by NCCL point-to-point inside the "
+                                  "timed region" if owners is not None else
+                                  "each rank keeps its own token range" if seqshard else "one GPU"),
                        "cuda_graph": bool(model.cuda_graphs),
                        "l2": (f"inputs (x {x_full.numel() * 4 / 1e6:.0f} MB) and per-step activations exceed the 126 MB L2"
                               if x_full.numel() * 4 > 126e6 else
@@ -508,9 +585,10 @@ def main():
             "attn_tflops_exact_equivalent": None if attn_exact_eq is None else round(attn_exact_eq, 1),
             "gemm_tflops": round(w_all["gemm_flops"] / (ms * 1e-3) / 1e12, 1),
             "kernels": kernels,
+            "kernels_ms_per_step_sum": round(sum(kms_l), 4),
             "roofline": {"kernel": dom, "bound": "tensor", "achieved": round(achieved, 1), "peak": peak,
                          "unit": "TFLOP/s", "frac": round(achieved / peak, 4), "traffic": traffic,
-                         "peak_source": f"{peak_src} bf16_tflops_sustained (fp16 dense rate)"},
+                         "peak_source": f"{peak_src} bf16_tflops (burst; fp16 dense rate)"},
             "cpu_baseline": cpu,
             "e2e": e2e,
             "gpu_launches": launches,

@@ -6,7 +6,9 @@ batch and prefix chunks through one GPU, src/implementations/extreme.py:136-204)
 * **Batch sharding** (independent samples): ``shard_samples`` assigns whole
   samples to ranks by a longest-processing-time rule on their algorithmic cost
   (ragged lengths make a contiguous split unbalanced); each rank then runs an
-  ordinary forward on its samples.  No data-path collective.
+  ordinary forward on its samples, with no collective inside the forward;
+  ``gather_batch_outputs`` then lands every sample's output rows in rank 0's
+  ``[B, N, d]`` buffer (NCCL point-to-point).
 * **Sequence sharding** (one long sequence per sample): ``SeqShardComm`` joins
   libtj's own NCCL communicator (the unique id travels over the existing
   torch.distributed group) and ``forward_seqshard`` runs rank r's token range
@@ -41,6 +43,55 @@ def shard_samples(lengths: Sequence[int], world: int, rank: int, d_model: int, f
         loads[r] += cost
         owner[i] = r
     return sorted(i for i, r in owner.items() if r == rank)
+
+
+def sample_owners(lengths: Sequence[int], world: int, d_model: int, ffn_dim: int) -> List[int]:
+    """Owning rank of every sample under ``shard_samples``'s assignment."""
+    owner = [0] * len(lengths)
+    for r in range(world):
+        for i in shard_samples(lengths, world, r, d_model, ffn_dim):
+            owner[i] = r
+    return owner
+
+
+def gather_batch_outputs(out_local: torch.Tensor, owners: Sequence[int], out_full=None, dst: int = 0):
+    """Assemble the batch-sharded forward's output on rank ``dst``.
+
+    ``out_local`` is this rank's ``[n_local, N, d]`` output (its samples in
+    ascending sample order, as ``shard_samples`` lists them); ``owners[i]`` is
+    the rank of sample i.  Rank ``dst`` receives every other rank's samples
+    straight into ``out_full`` ``[B, N, d]`` (made here when not given) with
+    point-to-point NCCL transfers -- one message per sample, issued as one
+    batch so they proceed concurrently -- and copies its own rows locally; it
+    returns ``out_full``.  The other ranks return None.  Every rank must call
+    this with the same ``owners``.  The reference returns the whole batch's
+    output from one forward (torch_transformer_benchmark.py:162-172); this is
+    the step that gives the sharded forward the same result tensor.
+    """
+    rank = dist.get_rank()
+    world = dist.get_world_size()
+    if len(owners) == 0 or max(owners) >= world:
+        raise ValueError("owners must name a rank of the process group for every sample")
+    mine = [i for i, r in enumerate(owners) if r == rank]
+    if out_local.shape[0] != len(mine):
+        raise ValueError(f"rank {rank} holds {out_local.shape[0]} samples, the assignment gives it {len(mine)}")
+    ops = []
+    if rank == dst:
+        if out_full is None:
+            out_full = torch.empty((len(owners),) + tuple(out_local.shape[1:]), dtype=out_local.dtype,
+                                   device=out_local.device)
+        for k, i in enumerate(mine):
+            out_full[i].copy_(out_local[k])
+        for i, r in enumerate(owners):
+            if r != dst:
+                ops.append(dist.P2POp(dist.irecv, out_full[i], r))
+    else:
+        for k, i in enumerate(mine):
+            ops.append(dist.P2POp(dist.isend, out_local[k].contiguous(), dst))
+    if ops:
+        for req in dist.batch_isend_irecv(ops):
+            req.wait()
+    return out_full if rank == dst else None
 
 
 def token_range(seq_len: int, world: int, rank: int) -> range:

@@ -66,3 +66,42 @@ def test_two_rank_sharding_partitions_and_balances():
 def test_token_range_rejects_uneven_split():
     with pytest.raises(ValueError):
         token_range(1000, 3, 0)
+
+
+def _gather_main(rank, world, port, results):
+    from techjam_b200.sharding import gather_batch_outputs, sample_owners
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        lengths = [5, 17, 3, 11, 9, 2, 13]
+        owners = sample_owners(lengths, world, 16, 64)
+        mine = [i for i, r in enumerate(owners) if r == rank]
+        assert mine == shard_samples(lengths, world, rank, 16, 64)
+        # every sample's "output" is its index, so rank 0 can check placement
+        out_local = torch.stack([torch.full((4, 3), float(i)) for i in mine]) if mine else torch.empty(0, 4, 3)
+        full = gather_batch_outputs(out_local, owners)
+        if rank == 0:
+            results.put((owners, full))
+        else:
+            assert full is None
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_batch_output_gather_lands_every_sample_on_rank0(world):
+    ctx = mp.get_context("spawn")
+    results = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_gather_main, args=(r, world, port, results)) for r in range(world)]
+    for p in procs:
+        p.start()
+    owners, full = results.get(timeout=120)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert len(set(owners)) == world  # every rank owns a sample
+    assert full.shape == (7, 4, 3)
+    for i in range(7):
+        assert torch.all(full[i] == float(i))
