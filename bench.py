@@ -452,13 +452,13 @@ def main():
 
     # batch sharding: every rank's output rows land in rank 0's [B, N, d] buffer
     owners = sample_owners(lengths, world, cfg.d_model, cfg.ffn_dim) if (world > 1 and not seqshard) else None
-    out_full = (torch.empty(cfg.batch_size, cfg.seq_len, cfg.d_model, dtype=torch.float32, device=dev)
+    out_full = (torch.zeros(cfg.batch_size, cfg.seq_len, cfg.d_model, dtype=torch.float32, device=dev)
                 if owners is not None and rank == 0 else None)
 
     def step(inp, msk):
         y = fwd(inp, msk)
-        if owners is not None:
-            gather_batch_outputs(y, owners, out_full)
+        if owners is not None:  # valid rows only; padded rows of out_full stay zero
+            gather_batch_outputs(y, owners, out_full, lengths=lengths)
         return y
 
     def barrier():
@@ -572,8 +572,8 @@ def main():
                        "layers": cfg.num_layers, "causal": cfg.causal, "padding_ratio": wl.padding_ratio,
                        "linear_scale": wl.linear_scale, "route": args.route,
                        "parallelism": parallelism,
-                       "output": ("gathered into rank 0's [B, N, d] buffer by NCCL point-to-point inside the "
-                                  "timed region" if owners is not None else
+                       "output": ("every sample's valid rows gathered into rank 0's zero-filled [B, N, d] buffer "
+                                  "by NCCL point-to-point inside the timed region" if owners is not None else
                                   "each rank keeps its own token range" if seqshard else "one GPU"),
                        "cuda_graph": bool(model.cuda_graphs),
                        "l2": (f"inputs (x {x_full.numel() * 4 / 1e6:.0f} MB) and per-step activations exceed the 126 MB L2"

@@ -231,11 +231,21 @@ TJ_API int tj_workspace_bytes_seqshard(const TjModel* model, const TjComm* comm,
    causal, no padding.  Token-local work runs on the shard; attention takes
    the guarded polynomial route (guard statistics all-reduced so every rank
    decides alike; each rank's state total all-gathered and folded into its
-   snapshots) or the exact flash route over all-gathered K/V.  Replaces the
-   single-GPU prefix streaming of forward_prefix_chunks
+   snapshots) or the exact flash route over all-gathered K/V.  The guard runs
+   on the first forward of a shard shape (batch, seq_local, world), with one
+   host read of its verdict per layer; later forwards reuse each layer's
+   verdict and coefficients without guard kernels or host synchronisation, as
+   the reference estimates sigma once per attention module and caches it
+   (src/implementations/extreme.py:297-301).  Reloading a layer's weights
+   re-evaluates it; every rank must do so alike.  Replaces the single-GPU
+   prefix streaming of forward_prefix_chunks
    (src/implementations/extreme.py:167-204). */
 TJ_API int tj_forward_seqshard(TjModel* model, TjComm* comm, const float* x, float* out, int batch, int seq_local,
                                int route, void* workspace, size_t workspace_bytes, void* stream);
+/* The sequence-sharded guard's cached verdict for a layer: 1 polynomial
+   route, 0 exact route, -1 not evaluated yet (no counterpart in the
+   reference beyond PolyOrFlashSelfAttention.route_name, extreme.py:268-272). */
+TJ_API int tj_seqshard_route(const TjModel* model, int layer, int* route);
 
 /* Guarded polynomial causal attention over Q,K,V fp16 [B,H,S,64] with no
    padding (lengths[b] == S), replacing PolyOrFlashSelfAttention.forward +

@@ -429,6 +429,13 @@ struct TjModel {
   int prof_n = 0;
   std::vector<cudaEvent_t> prof_ev;  // 2 per launch
   std::vector<int> prof_cls;
+  // Sequence-sharded polynomial route: the guard's verdict per layer, taken on
+  // the first forward of a shard shape and reused after it, as the reference
+  // estimates sigma once per attention module and caches it
+  // (src/implementations/extreme.py:297-301).  -1: not yet evaluated.
+  tj::PolyCtl* shard_ctl = nullptr;   // [num_layers] device copies of the guard result
+  std::vector<int> shard_route;        // host copy of each layer's admit flag
+  long long shard_key[3] = {0, 0, 0};  // batch, seq_local, world of the cached verdicts
 };
 
 namespace {
@@ -554,6 +561,12 @@ int tj_model_create(const TjConfig* cfg, TjModel** out) {
   e = cudaMalloc(&m->err, sizeof(int));
   if (e != cudaSuccess) { cudaFree(m->weights); delete m; return fail(TJ_ERR_CUDA, "cudaMalloc err: %s", cudaGetErrorString(e)); }
   cudaMemset(m->err, 0, sizeof(int));
+  e = cudaMalloc(&m->shard_ctl, sizeof(tj::PolyCtl) * c.num_layers);
+  if (e != cudaSuccess) {
+    cudaFree(m->weights); cudaFree(m->err); delete m;
+    return fail(TJ_ERR_CUDA, "cudaMalloc guard cache: %s", cudaGetErrorString(e));
+  }
+  m->shard_route.assign(c.num_layers, -1);
   uint8_t* p = static_cast<uint8_t*>(m->weights);
   auto take = [&](size_t bytes) { uint8_t* r = p; p += align_up(bytes, 256); return r; };
   m->layers.resize(c.num_layers);
@@ -582,6 +595,7 @@ int tj_model_destroy(TjModel* m) {
   for (cudaEvent_t e : m->prof_ev) cudaEventDestroy(e);
   cudaFree(m->weights);
   cudaFree(m->err);
+  cudaFree(m->shard_ctl);
   delete m;
   return TJ_OK;
 }
@@ -604,6 +618,7 @@ int tj_model_load_layer(TjModel* m, int layer, const TjLayerParams* P, void* str
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const size_t d = m->cfg.d_model, F = m->cfg.ffn_dim;
   TjLayerPacked& L = m->layers[layer];
+  m->shard_route[layer] = -1;  // new weights: the layer's guard verdict is re-evaluated
   TJ_CHECK(convert(P->q_weight, L.wqkv, d * d, st));
   TJ_CHECK(convert(P->k_weight, L.wqkv + d * d, d * d, st));
   TJ_CHECK(convert(P->v_weight, L.wqkv + 2 * d * d, d * d, st));
@@ -1013,8 +1028,8 @@ __global__ void fill_int_kernel(int* dst, int n, int value) {
 
 // Attention of one layer on a sequence shard: guarded polynomial route with a
 // state exchange, or exact flash over all-gathered K/V.
-int shard_attention(TjModel* m, TjComm* cm, ShardWorkspace& w, int B, int S_loc, int route, const tj::AttnParams& ap0,
-                    cudaStream_t st) {
+int shard_attention(TjModel* m, TjComm* cm, ShardWorkspace& w, int layer, int B, int S_loc, int route,
+                    const tj::AttnParams& ap0, cudaStream_t st) {
   const TjConfig& c = m->cfg;
   const int H = c.num_heads, hd = c.d_model / H, d = c.d_model;
   const int world = cm->world, rank = cm->rank;
@@ -1034,20 +1049,34 @@ int shard_attention(TjModel* m, TjComm* cm, ShardWorkspace& w, int B, int S_loc,
     pp.t_before = (float)rank * (float)S_loc;
     pp.total = w.total;
     pp.all_chunks = 1;
-    // guard over every shard's sample, decided identically everywhere
-    TJ_CUDA(cudaMemsetAsync(w.ctl, 0, sizeof(tj::PolyCtl), st));
-    tj::poly_guard_kernel<<<dim3(tj::kPolySample / 64, B * H), 256, 0, st>>>(pp);
-    TJ_CUDA(cudaGetLastError());
-    TJ_CHECK(nccl_check(cm, nc.AllReduce(&w.ctl->sum, &w.ctl->sum, 2, ncclFloat64, ncclSum, cm->comm, st), "guard sum"));
-    TJ_CHECK(nccl_check(cm, nc.AllReduce(&w.ctl->maxv, &w.ctl->maxv, 1, ncclFloat64, ncclMax, cm->comm, st), "guard max"));
-    tj::PolyParams pf = pp;
-    pf.guard_shards = world;  // the pooled sample covers every shard
-    tj::poly_guard_finalize<<<1, 1, 0, st>>>(pf);
-    TJ_CUDA(cudaGetLastError());
-    int flag = 0;
-    TJ_CUDA(cudaMemcpyAsync(&flag, &w.ctl->admit, sizeof(int), cudaMemcpyDeviceToHost, st));
-    TJ_CUDA(cudaStreamSynchronize(st));  // one host sync per layer: the exchange depends on the route
-    admit = flag != 0;
+    const long long key[3] = {B, S_loc, world};
+    if (std::memcmp(key, m->shard_key, sizeof(key)) != 0) {  // new shard shape: evaluate every layer again
+      std::memcpy(m->shard_key, key, sizeof(key));
+      m->shard_route.assign(c.num_layers, -1);
+    }
+    if (m->shard_route[layer] < 0) {
+      // guard over every shard's sample, decided identically everywhere; the
+      // host needs the verdict (the exchange depends on the route), so this
+      // first evaluation reads it back once and caches it for the layer
+      TJ_CUDA(cudaMemsetAsync(w.ctl, 0, sizeof(tj::PolyCtl), st));
+      tj::poly_guard_kernel<<<dim3(tj::kPolySample / 64, B * H), 256, 0, st>>>(pp);
+      TJ_CUDA(cudaGetLastError());
+      TJ_CHECK(nccl_check(cm, nc.AllReduce(&w.ctl->sum, &w.ctl->sum, 2, ncclFloat64, ncclSum, cm->comm, st), "guard sum"));
+      TJ_CHECK(nccl_check(cm, nc.AllReduce(&w.ctl->maxv, &w.ctl->maxv, 1, ncclFloat64, ncclMax, cm->comm, st), "guard max"));
+      tj::PolyParams pf = pp;
+      pf.guard_shards = world;  // the pooled sample covers every shard
+      tj::poly_guard_finalize<<<1, 1, 0, st>>>(pf);
+      TJ_CUDA(cudaGetLastError());
+      int flag = 0;
+      TJ_CUDA(cudaMemcpyAsync(&flag, &w.ctl->admit, sizeof(int), cudaMemcpyDeviceToHost, st));
+      TJ_CUDA(cudaStreamSynchronize(st));
+      TJ_CUDA(cudaMemcpyAsync(m->shard_ctl + layer, w.ctl, sizeof(tj::PolyCtl), cudaMemcpyDeviceToDevice, st));
+      m->shard_route[layer] = flag != 0 ? 1 : 0;
+    } else {
+      // cached verdict and coefficients: no guard kernels, no host synchronisation
+      TJ_CUDA(cudaMemcpyAsync(w.ctl, m->shard_ctl + layer, sizeof(tj::PolyCtl), cudaMemcpyDeviceToDevice, st));
+    }
+    admit = m->shard_route[layer] != 0;
     if (admit) {
       const int n_chunks = S_loc / tj::kPolyChunk;
       const uint64_t rows = (uint64_t)B * H * S_loc;
@@ -1148,6 +1177,13 @@ int tj_comm_destroy(TjComm* c) {
   return TJ_OK;
 }
 
+int tj_seqshard_route(const TjModel* m, int layer, int* route) {
+  if (!m || !route) return fail(TJ_ERR_INVALID, "null argument");
+  if (layer < 0 || layer >= m->cfg.num_layers) return fail(TJ_ERR_INVALID, "layer %d out of range", layer);
+  *route = m->shard_route[layer];
+  return TJ_OK;
+}
+
 int tj_workspace_bytes_seqshard(const TjModel* m, const TjComm* c, int B, int S_loc, int route, size_t* bytes) {
   if (!m || !c || !bytes || B <= 0 || S_loc <= 0) return fail(TJ_ERR_INVALID, "bad arguments");
   *bytes = carve_shard(m->cfg, B, S_loc, c->world, route, nullptr, nullptr);
@@ -1204,7 +1240,7 @@ int tj_forward_seqshard(TjModel* m, TjComm* cm, const float* x, float* out, int 
     }));
     gp.N = 3 * d; gp.K = d; gp.bias = L.bqkv;
     TJ_CHECK(timed_launch(m, TJ_K_QKV, 1, st, [&] { return launch_gemm_epi(tj::kEpiQKV, w.base.act, L.wqkv, gp, di.sms, st); }));
-    TJ_CHECK(shard_attention(m, cm, w, B, S_loc, route, ap, st));
+    TJ_CHECK(shard_attention(m, cm, w, l, B, S_loc, route, ap, st));
     gp.N = d; gp.K = d; gp.bias = L.bo; gp.out32 = out; gp.resid = resid_in;
     TJ_CHECK(timed_launch(m, TJ_K_OUT, 1, st, [&] { return launch_gemm_epi(tj::kEpiResid, w.base.act, L.wo, gp, di.sms, st); }));
     TJ_CHECK(timed_launch(m, TJ_K_LN, 1, st, [&] {

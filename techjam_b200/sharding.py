@@ -19,7 +19,7 @@ batch and prefix chunks through one GPU, src/implementations/extreme.py:136-204)
 from __future__ import annotations
 
 import ctypes
-from typing import List, Sequence
+from typing import List, Optional, Sequence
 
 import torch
 import torch.distributed as dist
@@ -54,7 +54,8 @@ def sample_owners(lengths: Sequence[int], world: int, d_model: int, ffn_dim: int
     return owner
 
 
-def gather_batch_outputs(out_local: torch.Tensor, owners: Sequence[int], out_full=None, dst: int = 0):
+def gather_batch_outputs(out_local: torch.Tensor, owners: Sequence[int], out_full=None, dst: int = 0,
+                         lengths: Optional[Sequence[int]] = None):
     """Assemble the batch-sharded forward's output on rank ``dst``.
 
     ``out_local`` is this rank's ``[n_local, N, d]`` output (its samples in
@@ -64,7 +65,10 @@ def gather_batch_outputs(out_local: torch.Tensor, owners: Sequence[int], out_ful
     point-to-point NCCL transfers -- one message per sample, issued as one
     batch so they proceed concurrently -- and copies its own rows locally; it
     returns ``out_full``.  The other ranks return None.  Every rank must call
-    this with the same ``owners``.  The reference returns the whole batch's
+    this with the same ``owners`` (and ``lengths``).  With ``lengths`` only
+    each sample's first ``lengths[i]`` rows (its valid prefix) move; the
+    padded rows of ``out_full`` are left as they are, so the caller passes a
+    zero-filled buffer (the forward writes padded rows as exact zeros).  The reference returns the whole batch's
     output from one forward (torch_transformer_benchmark.py:162-172); this is
     the step that gives the sharded forward the same result tensor.
     """
@@ -78,16 +82,20 @@ def gather_batch_outputs(out_local: torch.Tensor, owners: Sequence[int], out_ful
     ops = []
     if rank == dst:
         if out_full is None:
-            out_full = torch.empty((len(owners),) + tuple(out_local.shape[1:]), dtype=out_local.dtype,
+            out_full = torch.zeros((len(owners),) + tuple(out_local.shape[1:]), dtype=out_local.dtype,
                                    device=out_local.device)
         for k, i in enumerate(mine):
-            out_full[i].copy_(out_local[k])
+            n = out_local.shape[1] if lengths is None else int(lengths[i])
+            out_full[i, :n].copy_(out_local[k, :n])
         for i, r in enumerate(owners):
-            if r != dst:
-                ops.append(dist.P2POp(dist.irecv, out_full[i], r))
+            n = out_local.shape[1] if lengths is None else int(lengths[i])
+            if r != dst and n > 0:
+                ops.append(dist.P2POp(dist.irecv, out_full[i, :n], r))
     else:
         for k, i in enumerate(mine):
-            ops.append(dist.P2POp(dist.isend, out_local[k].contiguous(), dst))
+            n = out_local.shape[1] if lengths is None else int(lengths[i])
+            if n > 0:
+                ops.append(dist.P2POp(dist.isend, out_local[k, :n].contiguous(), dst))
     if ops:
         for req in dist.batch_isend_irecv(ops):
             req.wait()
@@ -160,4 +168,17 @@ def forward_seqshard(model: B200Transformer, comm: SeqShardComm, x_local: torch.
     with torch.cuda.device(x_local.device):
         _lib.call("tj_forward_seqshard", handle.ptr, comm.ptr, x_local.data_ptr(), out.data_ptr(), batch, s_loc,
                   _ROUTES[route], ws.data_ptr(), ws.numel(), ctypes.c_void_p(stream.cuda_stream))
+    return out
+
+
+def seqshard_routes(model: B200Transformer) -> List[int]:
+    """Each layer's cached sequence-sharded route: 1 polynomial, 0 exact, -1 not evaluated yet."""
+    handle = model._handle
+    if handle is None:
+        return [-1] * model.config.num_layers
+    out = []
+    for layer in range(model.config.num_layers):
+        r = ctypes.c_int()
+        _lib.call("tj_seqshard_route", handle.ptr, layer, ctypes.byref(r))
+        out.append(int(r.value))
     return out

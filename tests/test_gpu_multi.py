@@ -26,7 +26,7 @@ def _rank_main(rank, port, results):
     from oracle.reference_model import EncoderShape
     from techjam_b200.dispatcher import DispatchingTransformer
     from techjam_b200.harness import generate_random_case, seeded_model
-    from techjam_b200.sharding import SeqShardComm, forward_seqshard, token_range
+    from techjam_b200.sharding import SeqShardComm, forward_seqshard, seqshard_routes, token_range
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
@@ -47,6 +47,15 @@ def _rank_main(rank, port, results):
                 parts = [torch.empty_like(y) for _ in range(WORLD)]
                 dist.all_gather(parts, y)
                 outs[route] = torch.cat(parts, dim=1).cpu()
+                if route == "exact":
+                    assert seqshard_routes(model) == [-1]  # the exact route runs no guard
+            # the pooled guard admitted the polynomial route (sigma ~0.08 at 0.5x weights) ...
+            assert seqshard_routes(model) == [1]
+            # ... and a second forward reuses the cached verdict (no guard, no host read) with the same result
+            y2 = forward_seqshard(model, comm, x[:, rng.start:rng.stop].contiguous(), "auto")
+            parts = [torch.empty_like(y2) for _ in range(WORLD)]
+            dist.all_gather(parts, y2)
+            outs["auto_cached"] = torch.cat(parts, dim=1).cpu()
             torch.cuda.synchronize(dev)
             assert model.device_error() == 0
         if rank == 0:
@@ -91,6 +100,7 @@ def test_sequence_sharded_forward_two_gpus():
         torch.backends.cuda.matmul.allow_tf32 = old
     # exact route: same kernels, same key tiles in the same order -> identical
     assert torch.equal(outs["exact"], ref_exact)
+    assert torch.equal(outs["auto_cached"], outs["auto"])
     for route in ("exact", "auto"):
         v = check_outputs(ref, outs[route])
         assert v.passed, f"{route}: {v.failed_elements} failed, max_abs={v.max_abs_error:.3g}"

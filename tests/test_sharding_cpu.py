@@ -81,10 +81,11 @@ def _gather_main(rank, world, port, results):
         # every sample's "output" is its index, so rank 0 can check placement
         out_local = torch.stack([torch.full((4, 3), float(i)) for i in mine]) if mine else torch.empty(0, 4, 3)
         full = gather_batch_outputs(out_local, owners)
+        part = gather_batch_outputs(out_local, owners, lengths=[2] * len(lengths))  # valid prefixes only
         if rank == 0:
-            results.put((owners, full))
+            results.put((owners, full, part))
         else:
-            assert full is None
+            assert full is None and part is None
     finally:
         dist.destroy_process_group()
 
@@ -97,7 +98,7 @@ def test_batch_output_gather_lands_every_sample_on_rank0(world):
     procs = [ctx.Process(target=_gather_main, args=(r, world, port, results)) for r in range(world)]
     for p in procs:
         p.start()
-    owners, full = results.get(timeout=120)
+    owners, full, part = results.get(timeout=120)
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
@@ -105,3 +106,4 @@ def test_batch_output_gather_lands_every_sample_on_rank0(world):
     assert full.shape == (7, 4, 3)
     for i in range(7):
         assert torch.all(full[i] == float(i))
+        assert torch.all(part[i, :2] == float(i)) and torch.all(part[i, 2:] == 0)
