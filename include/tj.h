@@ -173,6 +173,11 @@ TJ_API int tj_profile_begin(TjModel* model, int max_launches);
 /* Synchronises on the recorded events and writes, per TjKernelClass, the
    summed device milliseconds and launch counts (arrays of TJ_K_COUNT). */
 TJ_API int tj_profile_end(TjModel* model, double* ms_by_class, long long* launches_by_class);
+/* Launches recorded while the stream was being captured into a CUDA graph
+   become event-record nodes that every replay records again.  After each
+   replay, this ADDS the replay's per-class milliseconds and launch counts to
+   the arrays, keeping the recording (finish with tj_profile_end). */
+TJ_API int tj_profile_collect(TjModel* model, double* ms_by_class, long long* launches_by_class);
 /* Total kernels this model has launched (all classes, profiling or not). */
 TJ_API int tj_launch_count(TjModel* model, long long* count);
 

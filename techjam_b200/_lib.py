@@ -61,6 +61,7 @@ SIGNATURES = {
     "tj_wait_selftest": (c_int, [c_void_p, c_void_p, c_void_p]),
     "tj_profile_begin": (c_int, [c_void_p, c_int]),
     "tj_profile_end": (c_int, [c_void_p, POINTER(ctypes.c_double), POINTER(ctypes.c_longlong)]),
+    "tj_profile_collect": (c_int, [c_void_p, POINTER(ctypes.c_double), POINTER(ctypes.c_longlong)]),
     "tj_launch_count": (c_int, [c_void_p, POINTER(ctypes.c_longlong)]),
     "tj_prepare_mask": (c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                 c_void_p]),

@@ -439,18 +439,27 @@ struct TjModel {
 };
 
 namespace {
+// Event record that also works while the stream is being captured into a CUDA
+// graph: there it becomes an event-record node, re-recorded at every replay.
+int record_event(cudaEvent_t ev, cudaStream_t st) {
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  TJ_CUDA(cudaStreamIsCapturing(st, &cs));
+  TJ_CUDA(cudaEventRecordWithFlags(ev, st, cs == cudaStreamCaptureStatusActive ? cudaEventRecordExternal
+                                                                              : cudaEventRecordDefault));
+  return TJ_OK;
+}
 // Runs one launcher, counting its kernels and bracketing it with an event pair
 // when profiling is active.
 template <class F>
 int timed_launch(TjModel* m, int cls, int kernels, cudaStream_t st, F&& launch) {
   if (m == nullptr) return launch();  // building-block call: no model to count or profile
   const bool rec = m->prof_on && m->prof_n < m->prof_max;
-  if (rec) TJ_CUDA(cudaEventRecord(m->prof_ev[2 * m->prof_n], st));
+  if (rec) TJ_CHECK(record_event(m->prof_ev[2 * m->prof_n], st));
   const int s = launch();
   if (s != TJ_OK) return s;
   m->launches += kernels;
   if (rec) {
-    TJ_CUDA(cudaEventRecord(m->prof_ev[2 * m->prof_n + 1], st));
+    TJ_CHECK(record_event(m->prof_ev[2 * m->prof_n + 1], st));
     m->prof_cls[m->prof_n] = cls;
     ++m->prof_n;
   }
@@ -883,6 +892,18 @@ int tj_wait_selftest(TjModel* m, int* err, void* stream) {
   if (word == nullptr) return fail(TJ_ERR_INVALID, "need a model or an error word");
   tj::wait_selftest_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(word);
   TJ_CUDA(cudaGetLastError());
+  return TJ_OK;
+}
+
+int tj_profile_collect(TjModel* m, double* ms, long long* counts) {
+  if (!m || !ms || !counts) return fail(TJ_ERR_INVALID, "null argument");
+  for (int i = 0; i < m->prof_n; ++i) {
+    TJ_CUDA(cudaEventSynchronize(m->prof_ev[2 * i + 1]));
+    float t = 0.f;
+    TJ_CUDA(cudaEventElapsedTime(&t, m->prof_ev[2 * i], m->prof_ev[2 * i + 1]));
+    ms[m->prof_cls[i]] += t;
+    counts[m->prof_cls[i]] += 1;
+  }
   return TJ_OK;
 }
 
