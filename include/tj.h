@@ -128,7 +128,9 @@ TJ_API int tj_forward(TjModel* model, const float* x, const uint8_t* valid_mask,
    exceeds the array are rejected with TJ_ERR_UNSUPPORTED.  The first call on
    a device resolves the array's device address; make that first call before
    any stream capture.  All calls share the one array: calls that overlap on
-   the GPU (different streams or threads) race. */
+   the GPU (different streams or threads) race.  The resolved address is kept
+   for the life of the device's context; after cudaDeviceReset, reload the
+   library before calling this again on that device. */
 #define TJ_NOALLOC_SCRATCH_BYTES (32u << 20)
 TJ_API int tj_forward_noalloc(TjModel* model, const float* x, const uint8_t* valid_mask, float* out, int batch,
                               int seq_len, int route, void* stream);

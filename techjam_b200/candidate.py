@@ -4,8 +4,9 @@
 reference's ``src/infra/candidate.py:15-130``, and ``validate_candidate_execution``
 its pre-allocation contract checks (:165-232), so that a module exposing
 ``CANDIDATE`` here can be consumed by the reference's loader
-(``load_candidate``, :133-162) once re-wrapped in its own class (see
-INTEGRATION.md for the two-line shim); ``TransformerConfig`` mirrors
+(``load_candidate``, :133-162) once re-wrapped in its own class (two lines:
+build the reference's ``CandidateSpec`` from this one's fields);
+``TransformerConfig`` mirrors
 ``torch_transformer_benchmark.py:29-56`` field for field so the model factory
 accepts either class.
 """

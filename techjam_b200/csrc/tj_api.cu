@@ -126,12 +126,17 @@ template <int BN, int EPI>
 int launch_gemm_bn(const CUtensorMap& ta, const CUtensorMap& tw, const tj::GemmParams& p, int sms, cudaStream_t st) {
   using Cfg = tj::GemmCfg<BN>;
   auto kern = tj::gemm_tc_kernel<BN, EPI>;
+  static std::mutex mu;
   static bool attr_set[64] = {};
   int dev = 0;
-  cudaGetDevice(&dev);
-  if (!attr_set[dev]) {
-    TJ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes));
-    attr_set[dev] = true;
+  TJ_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fail(TJ_ERR_NO_DEVICE, "device index %d out of range", dev);
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (!attr_set[dev]) {
+      TJ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes));
+      attr_set[dev] = true;
+    }
   }
   const long long m_tiles = (p.M + tj::kGemmBM - 1) / tj::kGemmBM;
   const long long n_tiles = (p.N + BN - 1) / BN;
@@ -149,9 +154,12 @@ int launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tw, const tj::Gem
                      cudaStream_t st) {
   using Cfg = tj::Gemm2Cfg;
   auto kern = tj::gemm_tc2_kernel<EPI>;
+  static std::mutex mu;
   static int max_pairs[64] = {};
   int dev = 0;
   TJ_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fail(TJ_ERR_NO_DEVICE, "device index %d out of range", dev);
+  std::unique_lock<std::mutex> lock(mu);
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -171,6 +179,7 @@ int launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tw, const tj::Gem
     max_pairs[dev] = n > 0 ? n : 1;
   }
   const int pairs = std::min(pair_tiles, max_pairs[dev]);
+  lock.unlock();
   if (pairs <= 0) return TJ_OK;
   cfg.gridDim = dim3(2 * pairs);
   TJ_CUDA(cudaLaunchKernelEx(&cfg, kern, ta, tw, p));
@@ -517,13 +526,18 @@ int launch_poly_route(const __half* q, const __half* k, const __half* v, __half*
   TJ_CHECK(make_map_f16(&tv, v, rows, 64, 128, 64, 128));
   const uint64_t snap_rows = (uint64_t)B * H * (n_chunks - pp.prefix_chunks) * tj::kPolyN;
   TJ_CHECK(make_map_f16(&tsn, snap, snap_rows, tj::kPolyFeat, tj::kPolyN, 64, 128));
+  static std::mutex mu;
   static bool attr_set[64] = {};
   int dev = 0;
   TJ_CUDA(cudaGetDevice(&dev));
-  if (!attr_set[dev]) {
-    TJ_CUDA(cudaFuncSetAttribute(tj::poly_update_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, tj::kUpdSmem));
-    TJ_CUDA(cudaFuncSetAttribute(tj::poly_apply_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, tj::kAppSmem));
-    attr_set[dev] = true;
+  if (dev < 0 || dev >= 64) return fail(TJ_ERR_NO_DEVICE, "device index %d out of range", dev);
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (!attr_set[dev]) {
+      TJ_CUDA(cudaFuncSetAttribute(tj::poly_update_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, tj::kUpdSmem));
+      TJ_CUDA(cudaFuncSetAttribute(tj::poly_apply_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, tj::kAppSmem));
+      attr_set[dev] = true;
+    }
   }
   TJ_CHECK(timed_launch(m, TJ_K_POLY, 2, st, [&]() -> int { return launch_poly_update(pp, tv, st); }));
   TJ_CHECK(timed_launch(m, TJ_K_POLY, 1, st, [&]() -> int {
@@ -780,7 +794,9 @@ void* g_noalloc_addr[64] = {};  // device address of g_noalloc_scratch, per devi
 
 // Host code cannot use g_noalloc_scratch's name as a device pointer (it is a
 // host-side stand-in); resolve the real address once per device, with that
-// device current.
+// device current.  The cached address belongs to the device's current
+// context: after cudaDeviceReset (which destroys it) the library must be
+// reloaded before tj_forward_noalloc is used on that device again.
 int noalloc_scratch(void** out) {
   int dev = 0;
   TJ_CUDA(cudaGetDevice(&dev));

@@ -353,15 +353,16 @@ TJ_DEV float row_max128(const uint32_t (&s)[128]) { return row_max<128>(s); }
 
 // 2^x for a pair of exponents x <= 16 (-inf and anything below -125 give
 // about 2^-125, i.e. nothing: the clamp keeps the integer exponent add
-// below from wrapping), on the FMA pipe instead of the SFU: x = n + f with
-// n = round(x) (x + 1.5*2^23 puts n in the low mantissa bits), f in
-// [-1/2, 1/2], 2^f from a degree-3 polynomial fitted (relative-error
-// minimax, Remez exchange) on that interval -- max relative error 7.5e-5,
-// below the fp16 rounding the values get next -- and 2^n added to the
-// exponent field as an integer (n << 23).
+// below from wrapping; a NaN passes the clamp and comes out NaN, as from the
+// SFU), on the FMA pipe instead of the SFU: x = n + f with n = round(x)
+// (x + 1.5*2^23 puts n in the low mantissa bits), f in [-1/2, 1/2], 2^f from
+// a degree-3 polynomial fitted (relative-error minimax, Remez exchange) on
+// that interval -- max relative error 7.5e-5, below the fp16 rounding the
+// values get next -- and 2^n added to the exponent field as an unsigned
+// integer (n << 23, wrapping modulo 2^32 by design).
 TJ_DEV float2 exp2_poly_x2(float x0, float x1) {
   constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
-  const uint64_t x = f32x2(fmaxf(x0, -125.0f), fmaxf(x1, -125.0f));
+  const uint64_t x = f32x2(x0 < -125.0f ? -125.0f : x0, x1 < -125.0f ? -125.0f : x1);
   const uint64_t j = fadd_x2(x, f32x2(kMagic, kMagic));
   const uint64_t n = fadd_x2(j, f32x2(-kMagic, -kMagic));
   const uint64_t f = ffma_x2(n, f32x2(-1.0f, -1.0f), x);
@@ -370,8 +371,8 @@ TJ_DEV float2 exp2_poly_x2(float x0, float x1) {
   q = ffma_x2(f, q, f32x2(0.6932609677314758f, 0.6932609677314758f));
   q = ffma_x2(f, q, f32x2(0.9999280571937561f, 0.9999280571937561f));
   const float2 pq = f32x2_split(q), pj = f32x2_split(j);
-  return make_float2(__int_as_float(__float_as_int(pj.x) * 8388608 + __float_as_int(pq.x)),
-                     __int_as_float(__float_as_int(pj.y) * 8388608 + __float_as_int(pq.y)));
+  return make_float2(__uint_as_float((__float_as_uint(pj.x) << 23) + __float_as_uint(pq.x)),
+                     __uint_as_float((__float_as_uint(pj.y) << 23) + __float_as_uint(pq.y)));
 }
 
 // P = 2^(S * sl2 - msub) for one N-column row: packed to fp16 pairs in place

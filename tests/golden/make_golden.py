@@ -1,9 +1,8 @@
 """Generate the golden fixtures that pin ``oracle/`` to the reference itself.
 
-Run in a checkout that has the reference repository available (default
-``/root/reference``; override with ``TJ_REFERENCE_ROOT``)::
+Run with ``TJ_REFERENCE_ROOT`` naming a checkout of the reference repository::
 
-    python tests/golden/make_golden.py
+    TJ_REFERENCE_ROOT=<reference checkout> python tests/golden/make_golden.py
 
 It imports the reference's own modules -- ``torch_transformer_benchmark``
 (``BaselineTransformer``, ``generate_random_case``) and
@@ -37,7 +36,9 @@ import numpy as np
 import torch
 
 HERE = Path(__file__).resolve().parent
-REF = Path(os.environ.get("TJ_REFERENCE_ROOT", "/root/reference"))
+if not os.environ.get("TJ_REFERENCE_ROOT"):
+    raise SystemExit("set TJ_REFERENCE_ROOT to a checkout of the reference repository")
+REF = Path(os.environ["TJ_REFERENCE_ROOT"])
 
 # name: (B, N, d, H, F, L, causal, padding_ratio, linear_scale, rows_kept or None=all)
 MODEL_CASES = {
@@ -179,7 +180,7 @@ def main():
     for name, spec in POLY_CASES.items():
         _poly_fixture(poly_ref, guard, name, spec)
         print("poly", name)
-    meta = {"reference_root": str(REF), "torch": torch.__version__,
+    meta = {"reference_root": "$TJ_REFERENCE_ROOT (a checkout of IceyFoxes/techjam)", "torch": torch.__version__,
             "model_cases": {k: list(v) for k, v in MODEL_CASES.items()},
             "poly_cases": {k: list(v) for k, v in POLY_CASES.items()},
             "checker_cases": sorted(_checker_cases())}

@@ -3,6 +3,7 @@ errors, a small C program links against ``libtj.so`` and its argument checks
 answer without a GPU (null pointers, unsupported head_dim, bad workspace
 queries) with a status code and a message, as a C/C++ host would see them."""
 
+import re
 import shutil
 import subprocess
 from pathlib import Path
@@ -62,4 +63,17 @@ def test_header_compiles_as_cxx(tmp_path):
     src.write_text('#include "tj.h"\nint main() { return tj_version() > 0 ? 0 : 1; }\n')
     res = subprocess.run(["g++", "-std=c++17", "-Wall", "-Werror", "-fsyntax-only", "-I", str(ROOT / "include"),
                           str(src)], capture_output=True, text=True)
+    assert res.returncode == 0, res.stderr
+
+
+@pytest.mark.skipif(shutil.which("gcc") is None, reason="needs gcc")
+def test_integration_example_compiles(tmp_path):
+    """The C host example of the integration guide compiles against tj.h as written."""
+    text = (ROOT / "INTEGRATION.md").read_text()
+    blocks = re.findall(r"```c\n(.*?)```", text, flags=re.S)
+    assert blocks, "no C example in the integration guide"
+    src = tmp_path / "example.c"
+    src.write_text(blocks[0])
+    res = subprocess.run(["gcc", "-std=c99", "-Wall", "-Wextra", "-Werror", "-fsyntax-only", "-I",
+                          str(ROOT / "include"), str(src)], capture_output=True, text=True)
     assert res.returncode == 0, res.stderr

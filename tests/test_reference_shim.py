@@ -1,7 +1,8 @@
-"""The drop-in boundary exercised with the reference's own classes (CPU; skipped
-where the reference checkout is absent, e.g. on the GPU box).
+"""The drop-in boundary exercised with the reference's own classes (CPU; runs
+when ``TJ_REFERENCE_ROOT`` names a checkout of the reference repository,
+skipped otherwise, e.g. on the GPU box).
 
-The two-line shim of INTEGRATION.md -- re-wrapping ``CANDIDATE`` in the
+The two-line shim -- re-wrapping ``CANDIDATE`` in the
 reference's ``CandidateSpec`` -- must pass the reference's ``load_candidate``
 and ``validate_candidate_execution``; the factory must accept the reference's
 ``TransformerConfig``; and the reference's strict ``copy_model_weights`` must
@@ -18,9 +19,9 @@ from pathlib import Path
 import pytest
 import torch
 
-REF = Path(os.environ.get("TJ_REFERENCE_ROOT", "/root/reference"))
-pytestmark = pytest.mark.skipif(not (REF / "torch_transformer_benchmark.py").exists(),
-                                reason="reference checkout not available")
+REF = Path(os.environ["TJ_REFERENCE_ROOT"]) if os.environ.get("TJ_REFERENCE_ROOT") else None
+pytestmark = pytest.mark.skipif(REF is None or not (REF / "torch_transformer_benchmark.py").exists(),
+                                reason="TJ_REFERENCE_ROOT does not name a reference checkout")
 
 
 @pytest.fixture(scope="module")
