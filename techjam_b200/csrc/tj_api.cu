@@ -328,11 +328,21 @@ int launch_layernorm(const float* x, const float* g, const float* b, void* out, 
   return TJ_OK;
 }
 
+// Mask -> per-sample lengths / flags and the live 128-row tiles.  With
+// counts/row_of/pack_of (varlen packing) the tiles are those of the packed
+// valid tokens and row_of / pack_of map packed rows to padded rows and back.
 int launch_prepare(const uint8_t* mask, int B, int S, int* lengths, uint8_t* general, int* tile_list, int* n_live,
-                   uint8_t* tile_live, int* sched, cudaStream_t st) {
-  tj::prep_lengths_kernel<<<B, 1024, 0, st>>>(mask, S, lengths, general, sched);
+                   uint8_t* tile_live, int* sched, int* counts, int* row_of, int* pack_of, cudaStream_t st) {
+  tj::prep_lengths_kernel<<<B, 1024, 0, st>>>(mask, S, lengths, general, sched, counts);
   TJ_CUDA(cudaGetLastError());
-  tj::prep_tiles_kernel<<<1, 1024, 0, st>>>(lengths, B, S, tile_list, n_live, tile_live);
+  if (row_of != nullptr) {
+    tj::prep_pack_kernel<<<B, 1024, 0, st>>>(mask, S, lengths, general, counts, pack_of, row_of);
+    TJ_CUDA(cudaGetLastError());
+    const int n_tiles = (int)(((long long)B * S + 127) / 128);
+    tj::prep_pack_tiles_kernel<<<1, 1024, 0, st>>>(counts, B, row_of, tile_list, n_live, tile_live, n_tiles);
+  } else {
+    tj::prep_tiles_kernel<<<1, 1024, 0, st>>>(lengths, B, S, tile_list, n_live, tile_live);
+  }
   TJ_CUDA(cudaGetLastError());
   return TJ_OK;
 }
@@ -345,6 +355,9 @@ struct Workspace {
   int* n_live;
   uint8_t* tile_live;
   int* sched;   // attention work scheduler (2 ints, zeroed by the mask prep)
+  int* counts;  // [B] valid tokens per sample
+  int* row_of;  // [M] padded row of each packed row (varlen packing)
+  int* pack_of; // [M] packed row of each padded row, -1 for padding
   __half* act;  // [M, d]: LN output, then attention context (reused)
   __half* q;
   __half* k;
@@ -388,6 +401,9 @@ size_t carve(const TjConfig& c, int B, int S, int route, uint8_t* base, Workspac
   t.n_live = reinterpret_cast<int*>(take(sizeof(int)));
   t.tile_live = take(tiles);
   t.sched = reinterpret_cast<int*>(take(2 * sizeof(int)));
+  t.counts = reinterpret_cast<int*>(take(sizeof(int) * B));
+  t.row_of = reinterpret_cast<int*>(take(sizeof(int) * M));
+  t.pack_of = reinterpret_cast<int*>(take(sizeof(int) * M));
   t.act = reinterpret_cast<__half*>(take(2 * M * c.d_model));
   t.q = reinterpret_cast<__half*>(take(2 * M * c.d_model));
   t.k = reinterpret_cast<__half*>(take(2 * M * c.d_model));
@@ -706,10 +722,18 @@ int tj_forward(TjModel* m, const float* x, const uint8_t* mask, float* out, int 
   const int d = c.d_model, H = c.num_heads, hd = d / H, F = c.ffn_dim;
   const int M = B * S;
 
-  TJ_CHECK(timed_launch(m, TJ_K_PREP, 2, st, [&] {
-    return launch_prepare(mask, B, S, w.lengths, w.general, w.tile_list, w.n_live, w.tile_live, w.sched, st);
+  // Varlen token packing: with padding present (a mask) the LayerNorm
+  // outputs, the GEMMs' fp16 rows and the attention context hold only the
+  // valid tokens, back to back; the FP32 residual stream, Q/K/V and the output
+  // keep the padded [B, S] layout (the polynomial route, for unpadded long
+  // sequences only, keeps the padded rows throughout).
+  const bool packed = mask != nullptr && w.poly_ctl == nullptr;
+  TJ_CHECK(timed_launch(m, TJ_K_PREP, packed ? 3 : 2, st, [&] {
+    return launch_prepare(mask, B, S, w.lengths, w.general, w.tile_list, w.n_live, w.tile_live, w.sched, w.counts,
+                          packed ? w.row_of : nullptr, w.pack_of, st);
   }));
-  tj::RowValidity rv{w.lengths, mask, S, (long long)M};
+  tj::RowValidity rv{w.lengths, mask, S, (long long)M, packed ? w.pack_of : nullptr};
+  tj::RowValidity rv_out{w.lengths, mask, S, (long long)M, nullptr};  // final LayerNorm: every padded row
 
   tj::GemmParams gp{};
   gp.M = M;
@@ -721,8 +745,10 @@ int tj_forward(TjModel* m, const float* x, const uint8_t* mask, float* out, int 
   gp.q = w.q; gp.k = w.k; gp.v = w.v;
   gp.heads = H; gp.head_dim = hd; gp.d_model = d;
   gp.err = m->err;
+  gp.row_of = packed ? w.row_of : nullptr;
 
   tj::AttnParams ap{};
+  ap.pack_of = packed ? w.pack_of : nullptr;
   ap.lengths = w.lengths;
   ap.mask = mask;
   ap.general = w.general;
@@ -773,7 +799,7 @@ int tj_forward(TjModel* m, const float* x, const uint8_t* mask, float* out, int 
   }
   // final LayerNorm in place; every invalid row becomes exactly 0
   TJ_CHECK(timed_launch(m, TJ_K_LN_FINAL, 1, st, [&] {
-    return launch_layernorm(out, m->final_g, m->final_b, out, false, true, d, eps, rv, w.tile_live, st);
+    return launch_layernorm(out, m->final_g, m->final_b, out, false, true, d, eps, rv_out, w.tile_live, st);
   }));
   return TJ_OK;
 }
@@ -934,14 +960,14 @@ int tj_prepare_mask(const uint8_t* mask, int B, int S, int* lengths, uint8_t* ge
                     uint8_t* tile_live, void* stream) {
   if (!lengths || !general || !tile_list || !n_live || !tile_live) return fail(TJ_ERR_INVALID, "null argument");
   if (B <= 0 || S <= 0) return fail(TJ_ERR_INVALID, "batch and seq_len must be positive");
-  return launch_prepare(mask, B, S, lengths, general, tile_list, n_live, tile_live, nullptr,
-                        static_cast<cudaStream_t>(stream));
+  return launch_prepare(mask, B, S, lengths, general, tile_list, n_live, tile_live, nullptr, nullptr, nullptr,
+                        nullptr, static_cast<cudaStream_t>(stream));
 }
 
 int tj_layernorm(const float* x, const float* g, const float* b, int B, int S, int d, float eps, void* out,
                  int out_fp16, const int* lengths, const uint8_t* mask, const uint8_t* tile_live, void* stream) {
   if (!x || !g || !b || !out || !lengths || !tile_live) return fail(TJ_ERR_INVALID, "null argument");
-  tj::RowValidity rv{lengths, mask, S, (long long)B * S};
+  tj::RowValidity rv{lengths, mask, S, (long long)B * S, nullptr};
   return launch_layernorm(x, g, b, out, out_fp16 != 0, out_fp16 == 0, d, eps, rv, tile_live,
                           static_cast<cudaStream_t>(stream));
 }
@@ -1257,7 +1283,7 @@ int tj_forward_seqshard(TjModel* m, TjComm* cm, const float* x, float* out, int 
     TJ_CUDA(cudaGetLastError());
     return TJ_OK;
   }));
-  tj::RowValidity rv{w.base.lengths, nullptr, S_loc, (long long)M};
+  tj::RowValidity rv{w.base.lengths, nullptr, S_loc, (long long)M, nullptr};
   tj::GemmParams gp{};
   gp.M = M; gp.seq = S_loc; gp.lengths = w.base.lengths; gp.mask = nullptr;
   gp.tile_list = w.base.tile_list; gp.n_live = w.base.n_live;

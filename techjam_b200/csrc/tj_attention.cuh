@@ -55,7 +55,17 @@ struct AttnParams {
   // before the launch and zero again after it (the last CTA to finish resets
   // both).  Null: item i goes to CTA i % grid.
   int* sched;
+  // Varlen packing: the context row of token (b, n) is pack_of[b*S + n]
+  // (-1: padding, not written).  Null: row b*S + n.
+  const int* pack_of;
 };
+
+// Context row of query token (b, qrow), or -1 when it is not written.
+TJ_DEV long long ctx_row(const AttnParams& p, int b, int qrow) {
+  if (qrow >= p.S) return -1;
+  const long long r = (long long)b * p.S + qrow;
+  return p.pack_of != nullptr ? (long long)__ldg(p.pack_of + r) : r;
+}
 
 template <int HD>
 struct AttnCfg {
@@ -351,8 +361,9 @@ __global__ void __launch_bounds__(AttnCfg<HD>::kThreads, 1)
     if (ok && nkv_t > 0 && mbar_wait(o_final + t, 0, p.err, kErrAttnSoftmax)) {
       tc_fence_after();
       const float inv = l_run > 0.0f ? 1.0f / l_run : 0.0f;
-      __half* dst = p.ctx + ((size_t)b * p.S + qrow) * p.d_model + (size_t)h * HD;
-      const bool store = qrow < p.S;
+      const long long crow = ctx_row(p, b, qrow);
+      __half* dst = p.ctx + (crow < 0 ? 0 : crow) * (size_t)p.d_model + (size_t)h * HD;
+      const bool store = crow >= 0;
 #pragma unroll
       for (int c = 0; c < HD / 32; ++c) {
         uint32_t o[32];
@@ -774,7 +785,8 @@ __global__ void __launch_bounds__(384, 1)
       cs += nkv_t;
       pending = true;
       prev_inv = l_run > 0.0f ? 1.0f / l_run : 0.0f;
-      prev_dst = qrow < p.S ? p.ctx + ((size_t)it.b * p.S + qrow) * p.d_model + (size_t)it.h * HD : nullptr;
+      const long long crow = ctx_row(p, it.b, qrow);
+      prev_dst = crow >= 0 ? p.ctx + (size_t)crow * p.d_model + (size_t)it.h * HD : nullptr;
     }
     if (ok && pending && mbar_wait(o_final + t, co & 1, p.err, kErrAttnSoftmax)) {
       tc_fence_after();

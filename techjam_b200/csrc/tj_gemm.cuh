@@ -38,6 +38,11 @@ struct GemmParams {
   float* out32;
   const float* resid;
   int* err;
+  // Packed rows (varlen): GEMM row r is the r-th valid token, at padded row
+  // row_of[r] of the [B*seq] layout (-1 past the last valid token).  The
+  // fp16 operand / output rows are packed; the QKV scatter and the FP32
+  // residual stream go through row_of.  Null: rows are the padded rows.
+  const int* row_of;
 };
 
 constexpr int kGemmBM = 128;
@@ -62,8 +67,19 @@ struct GemmCfg {
   static constexpr int kEpiThreads = 256;
 };
 
+// Padded row of GEMM row `row`, or -1 for a row that holds no valid token.
+TJ_DEV int src_row(const GemmParams& p, int row) {
+  if (row >= p.M) return -1;
+  if (p.row_of != nullptr) return __ldg(p.row_of + row);
+  const int b = row / p.seq;
+  const int n = row - b * p.seq;
+  if (n >= __ldg(p.lengths + b)) return -1;
+  return (p.mask == nullptr || __ldg(p.mask + row) != 0) ? row : -1;
+}
+
 TJ_DEV bool row_is_valid(const GemmParams& p, int row) {
   if (row >= p.M) return false;
+  if (p.row_of != nullptr) return __ldg(p.row_of + row) >= 0;
   const int b = row / p.seq;
   const int n = row - b * p.seq;
   if (n >= __ldg(p.lengths + b)) return false;
@@ -110,10 +126,17 @@ TJ_DEV bool f16_epilogue(const GemmParams& p, uint32_t taddr, int row0, int colh
   const bool my_valid = live && row_is_valid(p, row0 + lane);  // this thread's accumulator row
   const int piece = lane & 3;
   uint32_t in_m = 0;  // bit 2h+i: store-side row row0 + 16h + 8i + lane/4 is < M
+  int srow[4];         // QKV: that row's padded token position (fetched under the main loop)
   if (live) {
 #pragma unroll
-    for (int k = 0; k < 4; ++k)
-      if (row0 + 8 * k + (lane >> 2) < p.M) in_m |= 1u << k;
+    for (int k = 0; k < 4; ++k) {
+      const int row = row0 + 8 * k + (lane >> 2);
+      srow[k] = row;
+      if (row < p.M) {
+        in_m |= 1u << k;
+        if (EPI == kEpiQKV && p.row_of != nullptr) srow[k] = __ldg(p.row_of + row);
+      }
+    }
   }
   if (!wait_acc()) return false;
   tc_fence_after();
@@ -168,15 +191,20 @@ TJ_DEV bool f16_epilogue(const GemmParams& p, uint32_t taddr, int row0, int colh
         if ((in_m >> (2 * h + i)) & 1u) {
           const uint4 val = *reinterpret_cast<const uint4*>(stage + rr * 80 + 16 * piece);
           const int row = row0 + 16 * h + rr;
-          __half* dst;
+          __half* dst = nullptr;
           if constexpr (EPI == kEpiQKV) {
-            const int b = row / p.seq;
-            const int n = row - b * p.seq;
-            dst = col_base + (((size_t)b * p.heads + head) * p.seq + n) * p.head_dim + dim0;
+            // packed rows scatter to their token's padded position; a packed
+            // row past the last valid token has none
+            const int pr = srow[2 * h + i];
+            if (pr >= 0) {
+              const int b = pr / p.seq;
+              const int n = pr - b * p.seq;
+              dst = col_base + (((size_t)b * p.heads + head) * p.seq + n) * p.head_dim + dim0;
+            }
           } else {
             dst = col_base + (size_t)row * p.N;
           }
-          *reinterpret_cast<uint4*>(dst + 8 * piece) = val;
+          if (dst != nullptr) *reinterpret_cast<uint4*>(dst + 8 * piece) = val;
         }
       }
       __syncwarp();
@@ -197,14 +225,23 @@ TJ_DEV bool resid_epilogue(const GemmParams& p, uint32_t taddr, int row0, int co
                            int lane, WaitAcc&& wait_acc) {
   const int sub = lane >> 3;
   const int c4 = 4 * (lane & 7);
-  uint32_t in_m = 0, valid = 0;  // bit i: row row0 + 4i + sub is < M / valid
+  uint32_t in_m = 0, valid = 0;  // bit i: row row0 + 4i + sub is written / valid
+  int prow[8];                    // its row of the FP32 residual stream
+#pragma unroll
+  for (int i = 0; i < 8; ++i) prow[i] = row0 + 4 * i + sub;
   if (live) {
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const int row = row0 + 4 * i + sub;
       if (row < p.M) {
-        in_m |= 1u << i;
-        if (row_is_valid(p, row)) valid |= 1u << i;
+        const int sr = src_row(p, row);
+        if (p.row_of != nullptr) {
+          prow[i] = sr;  // packed rows: only valid tokens have a residual row to write
+          if (sr >= 0) in_m |= 1u << i;
+        } else {
+          in_m |= 1u << i;  // padded rows: invalid ones are written as zeros
+        }
+        if (sr >= 0) valid |= 1u << i;
       }
     }
   }
@@ -212,8 +249,9 @@ TJ_DEV bool resid_epilogue(const GemmParams& p, uint32_t taddr, int row0, int co
   // still run (one bulk prefetch, no registers); the register loads below
   // then wait on L2 rather than DRAM.  Only for short reductions (out-proj):
   // with K = 4096 the tile's own operand stream gains more from the L2.
-  if (p.K <= 1024 && live && colh < p.N && row_is_valid(p, row0 + lane)) {
-    const float* src = p.resid + (size_t)(row0 + lane) * p.N + colh;
+  const int my_src = live && colh < p.N ? src_row(p, row0 + lane) : -1;
+  if (p.K <= 1024 && my_src >= 0) {
+    const float* src = p.resid + (size_t)my_src * p.N + colh;
     const int bytes = min(kChunks * 32, p.N - colh) * 4;
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
   }
@@ -223,7 +261,7 @@ TJ_DEV bool resid_epilogue(const GemmParams& p, uint32_t taddr, int row0, int co
     if (colh + c * 32 >= p.N) return;
 #pragma unroll
     for (int i = 0; i < 8; ++i)
-      if ((valid >> i) & 1u) r[i] = *reinterpret_cast<const float4*>(p.resid + (size_t)(row0 + 4 * i + sub) * p.N + col);
+      if ((valid >> i) & 1u) r[i] = *reinterpret_cast<const float4*>(p.resid + (size_t)prow[i] * p.N + col);
   };
   if (live) prefetch(0, res[0]);  // overlaps the tile's last MMAs
   if (!wait_acc()) return false;
@@ -259,7 +297,7 @@ TJ_DEV bool resid_epilogue(const GemmParams& p, uint32_t taddr, int row0, int co
             const float4 r = res[c & 1][ii];
             o = make_float4(a.x + b4.x + r.x, a.y + b4.y + r.y, a.z + b4.z + r.z, a.w + b4.w + r.w);
           }
-          *reinterpret_cast<float4*>(p.out32 + (size_t)(row0 + 16 * h + rr) * p.N + col0 + c4) = o;
+          *reinterpret_cast<float4*>(p.out32 + (size_t)prow[ii] * p.N + col0 + c4) = o;
         }
       }
       __syncwarp();

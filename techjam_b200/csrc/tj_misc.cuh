@@ -11,13 +11,19 @@ constexpr int kTileRows = 128;
 // not a right-padded prefix.  mask == null means every position is valid.
 // sched (nullable): the attention scheduler's two words, zeroed here so that a
 // forward starts from a clean scheduler even after an aborted launch.
+// counts (nullable): valid tokens per sample.
 __global__ void __launch_bounds__(1024) prep_lengths_kernel(const uint8_t* __restrict__ mask, int S,
                                                              int* __restrict__ lengths,
-                                                             uint8_t* __restrict__ general, int* __restrict__ sched) {
+                                                             uint8_t* __restrict__ general, int* __restrict__ sched,
+                                                             int* __restrict__ counts) {
   const int b = blockIdx.x;
   if (sched != nullptr && b == 0 && threadIdx.x < 2) sched[threadIdx.x] = 0;
   if (mask == nullptr) {
-    if (threadIdx.x == 0) { lengths[b] = S; general[b] = 0; }
+    if (threadIdx.x == 0) {
+      lengths[b] = S;
+      general[b] = 0;
+      if (counts != nullptr) counts[b] = S;
+    }
     return;
   }
   const uint8_t* m = mask + (size_t)b * S;
@@ -56,7 +62,11 @@ __global__ void __launch_bounds__(1024) prep_lengths_kernel(const uint8_t* __res
       last = max(last, __shfl_xor_sync(0xffffffffu, last, o));
       count += __shfl_xor_sync(0xffffffffu, count, o);
     }
-    if (l == 0) { lengths[b] = last; general[b] = (count != last) ? 1 : 0; }
+    if (l == 0) {
+      lengths[b] = last;
+      general[b] = (count != last) ? 1 : 0;
+      if (counts != nullptr) counts[b] = count;
+    }
   }
 }
 
@@ -109,11 +119,106 @@ __global__ void prep_tiles_kernel(const int* __restrict__ lengths, int B, int S,
   if (threadIdx.x == 0) *n_live = s_base;
 }
 
+// Varlen token packing: the valid tokens of the [B*S] rows, sample by sample
+// in position order, become packed rows 0..T_v-1.  One block per sample:
+// pack_of[b*S + n] = packed row of token (b, n) or -1; row_of[packed] = b*S + n.
+// A right-padded sample's tokens are its first lengths[b] positions; a
+// general mask's are found with a block-wide scan.
+__global__ void __launch_bounds__(1024) prep_pack_kernel(const uint8_t* __restrict__ mask, int S,
+                                                          const int* __restrict__ lengths,
+                                                          const uint8_t* __restrict__ general,
+                                                          const int* __restrict__ counts, int* __restrict__ pack_of,
+                                                          int* __restrict__ row_of) {
+  const int b = blockIdx.x;
+  __shared__ int s_warp[32];
+  __shared__ int s_off, s_base;
+  // exclusive prefix of the earlier samples' token counts
+  int part = 0;
+  for (int i = threadIdx.x; i < b; i += blockDim.x) part += counts[i];
+  for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+  const int l = threadIdx.x & 31, w = threadIdx.x >> 5;
+  if (l == 0) s_warp[w] = part;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int t = 0;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) t += s_warp[i];
+    s_off = t;
+    s_base = 0;
+  }
+  __syncthreads();
+  const int off = s_off;
+  const long long row0 = (long long)b * S;
+  if (mask == nullptr || general[b] == 0) {
+    const int len = lengths[b];
+    for (int n = threadIdx.x; n < S; n += blockDim.x) {
+      const int k = n < len ? off + n : -1;
+      pack_of[row0 + n] = k;
+      if (k >= 0) row_of[k] = (int)(row0 + n);
+    }
+    return;
+  }
+  for (int start = 0; start < S; start += blockDim.x) {
+    __syncthreads();  // s_warp reuse
+    const int n = start + threadIdx.x;
+    const int v = n < S && mask[row0 + n] != 0 ? 1 : 0;
+    int incl = v;
+    for (int o = 1; o < 32; o <<= 1) {
+      const int u = __shfl_up_sync(0xffffffffu, incl, o);
+      if (l >= o) incl += u;
+    }
+    if (l == 31) s_warp[w] = incl;
+    __syncthreads();
+    if (w == 0) {
+      int x = s_warp[l];
+      for (int o = 1; o < 32; o <<= 1) {
+        const int u = __shfl_up_sync(0xffffffffu, x, o);
+        if (l >= o) x += u;
+      }
+      s_warp[l] = x;
+    }
+    __syncthreads();
+    const int excl = incl - v + (w > 0 ? s_warp[w - 1] : 0);
+    if (n < S) {
+      const int k = v ? off + s_base + excl : -1;
+      pack_of[row0 + n] = k;
+      if (k >= 0) row_of[k] = (int)(row0 + n);
+    }
+    __syncthreads();
+    if (threadIdx.x == blockDim.x - 1) s_base += excl + v;
+  }
+}
+
+// Live tiles of the packed rows: tiles 0 .. ceil(T_v/128)-1, and row_of = -1
+// for the packed rows of the last tile past T_v.  One block.
+__global__ void prep_pack_tiles_kernel(const int* __restrict__ counts, int B, int* __restrict__ row_of,
+                                       int* __restrict__ tile_list, int* __restrict__ n_live,
+                                       uint8_t* __restrict__ tile_live, int n_tiles_all) {
+  __shared__ int s_warp[32];
+  int part = 0;
+  for (int i = threadIdx.x; i < B; i += blockDim.x) part += counts[i];
+  for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+  if ((threadIdx.x & 31) == 0) s_warp[threadIdx.x >> 5] = part;
+  __syncthreads();
+  int tv = 0;
+  for (int i = 0; i < (int)(blockDim.x >> 5); ++i) tv += s_warp[i];
+  const int tiles = (tv + kTileRows - 1) / kTileRows;
+  for (int t = threadIdx.x; t < n_tiles_all; t += blockDim.x) {
+    tile_list[t] = t;
+    tile_live[t] = t < tiles ? 1 : 0;
+  }
+  for (int r = tv + (int)threadIdx.x; r < tiles * kTileRows; r += blockDim.x) row_of[r] = -1;
+  if (threadIdx.x == 0) *n_live = tiles;
+}
+
+// Row addressing of the LayerNorm kernels: padded row r is token (r / S,
+// r % S), valid inside the sample's prefix (and its mask).  Its output row is
+// r, or pack_of[r] with varlen packing (then invalid rows are not written).
 struct RowValidity {
   const int* lengths;
   const uint8_t* mask;
   int S;
   long long M;
+  const int* pack_of;
   __device__ bool operator()(long long row) const {
     if (row >= M) return false;
     const int b = (int)(row / S);
@@ -135,7 +240,9 @@ __global__ void __launch_bounds__(256) layernorm_kernel(const float* __restrict_
   const int lane = threadIdx.x & 31;
   if (row >= valid.M) return;
   const bool ok = valid(row);
-  if (!ok && !ALL_ROWS && tile_live[row / kTileRows] == 0) return;
+  if (!ok && (valid.pack_of != nullptr || (!ALL_ROWS && tile_live[row / kTileRows] == 0))) return;
+  // output row: issued now, used only by the stores at the end
+  const long long orow = valid.pack_of != nullptr ? (long long)__ldg(valid.pack_of + row) : row;
   const int nvec = d >> 2;
   float4 v[VPL];
   if (ok) {
@@ -186,9 +293,9 @@ __global__ void __launch_bounds__(256) layernorm_kernel(const float* __restrict_
         uint2 w;
         w.x = pack_half2(v[i].x, v[i].y);
         w.y = pack_half2(v[i].z, v[i].w);
-        reinterpret_cast<uint2*>(static_cast<__half*>(out) + row * d)[c] = w;
+        reinterpret_cast<uint2*>(static_cast<__half*>(out) + orow * d)[c] = w;
       } else {
-        reinterpret_cast<float4*>(static_cast<float*>(out) + row * d)[c] = v[i];
+        reinterpret_cast<float4*>(static_cast<float*>(out) + orow * d)[c] = v[i];
       }
     }
   }

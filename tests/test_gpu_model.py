@@ -217,3 +217,21 @@ def test_cuda_graph_replay():
         third = cand(x, mask)
         assert torch.equal(third, eager(x, mask))
         assert cand.graph_kernel_launches > 0
+
+
+def test_varlen_packing_is_exact():
+    """Varlen packing (valid tokens back to back through LayerNorm, the GEMMs
+    and the attention context) changes no arithmetic: each sample's rows of a
+    padded batch equal that sample run alone, unpadded, bit for bit; an
+    all-valid mask gives the no-mask result; and the batch passes the oracle."""
+    cfg = EncoderShape(3, 640, 256, 8, 1024, 2, True)
+    oracle, cand = _models(cfg, 1.0)
+    with torch.inference_mode():
+        x, mask = generate_random_case(cfg, DEV, torch.float32, 21, 0.6)
+        full = cand(x, mask)
+        _assert_pass(oracle(x, mask), full, mask, cand)
+        for b, n in enumerate(mask.sum(1).tolist()):
+            alone = cand(x[b:b + 1, :n].contiguous(), None)
+            assert torch.equal(full[b, :n], alone[0]), f"sample {b} (length {n}) differs from its solo run"
+        assert torch.equal(cand(x, torch.ones_like(mask)), cand(x, None))
+        assert cand.device_error() == 0
