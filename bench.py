@@ -502,7 +502,7 @@ def main():
         ms_no_gather = timed(fwd) if owners is not None else ms
 
         # ---- per-kernel pass (event pairs around every launch)
-        per_fwd = 12 * cfg.num_layers + 4  # upper bound incl. the polynomial route's launches
+        per_fwd = 16 * cfg.num_layers + 16  # upper bound incl. the polynomial route's launches
         graphs_were = model.cuda_graphs
         model.cuda_graphs = False
         kms = (ctypes.c_double * 9)()

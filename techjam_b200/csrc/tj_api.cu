@@ -1027,6 +1027,10 @@ struct TjComm {
   int world = 1;
   int timeout_ms = 60000;
   bool broken = false;
+  // Exchange stream of the polynomial route: the head groups' state
+  // all-gathers and fix-ups run here under the next groups' update kernels.
+  cudaStream_t side = nullptr;
+  std::vector<cudaEvent_t> events;
 };
 
 namespace {
@@ -1051,6 +1055,9 @@ struct ShardWorkspace {
   __half* kg;       // [world][B][H][S_loc][64]: every shard's K (exact route)
   __half* vg;
 };
+
+// Head groups the sequence-sharded polynomial route pipelines its state exchange over.
+constexpr int kShardExchangeGroups = 4;
 
 bool shard_poly_eligible(const TjConfig& c, int S_loc, int world, int route) {
   if (route == TJ_ROUTE_EXACT || !c.causal || c.d_model / c.num_heads != 64) return false;
@@ -1151,20 +1158,64 @@ int shard_attention(TjModel* m, TjComm* cm, ShardWorkspace& w, int layer, int B,
       TJ_CHECK(make_map_f16(&tsn, w.snap, snap_rows, tj::kPolyFeat, tj::kPolyN, 64, 128));
       TJ_CUDA(cudaFuncSetAttribute(tj::poly_update_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, tj::kUpdSmem));
       TJ_CUDA(cudaFuncSetAttribute(tj::poly_apply_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, tj::kAppSmem));
-      TJ_CHECK(timed_launch(m, TJ_K_POLY, 2, st, [&]() -> int { return launch_poly_update(pp, tv, st); }));
-      const size_t state = (size_t)B * H * tj::kPolyN * tj::kPolyFeat;
-      TJ_CHECK(nccl_check(cm, nc.AllGather(w.total, w.gathered, state, ncclFloat32, cm->comm, st), "state all-gather"));
-      if (rank > 0) {
-        tj::poly_fixup_kernel<<<1184, 256, 0, st>>>(w.gathered, rank, B * H, w.snap, n_chunks - pp.prefix_chunks,
-                                                     pp.prefix_chunks, pp.t_before);
-        TJ_CUDA(cudaGetLastError());
+      // The state exchange is pipelined over groups of heads: group g's
+      // update kernel runs on the compute stream, then its all-gather and
+      // fix-up on the exchange stream while groups g+1.. update; each group's
+      // apply waits only for its own fix-up.  Only the last group's exchange
+      // is exposed.  Every rank issues the same collectives in the same order.
+      const int BH = B * H;
+      const int groups = std::min(kShardExchangeGroups, BH);
+      const int G = (BH + groups - 1) / groups;
+      const size_t per = (size_t)tj::kPolyN * tj::kPolyFeat;
+      if (cm->side == nullptr) TJ_CUDA(cudaStreamCreateWithFlags(&cm->side, cudaStreamNonBlocking));
+      while ((int)cm->events.size() < 2 * groups) {
+        cudaEvent_t e;
+        TJ_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+        cm->events.push_back(e);
       }
       TJ_CHECK(timed_launch(m, TJ_K_POLY, 1, st, [&]() -> int {
-        tj::poly_apply_kernel<<<dim3((n_chunks - pp.prefix_chunks) * 4, B * H), tj::kAppThreads, tj::kAppSmem, st>>>(tq, tk, tv,
-                                                                                                       tsn, pp);
+        tj::poly_k_transpose_kernel<<<dim3(pp.S / 64, BH), 256, 0, st>>>(pp.k, pp.kt, pp.S);
         TJ_CUDA(cudaGetLastError());
         return TJ_OK;
       }));
+      CUtensorMap tkt;
+      TJ_CHECK(make_map_f16(&tkt, pp.kt, (uint64_t)BH * 64, (uint64_t)pp.S, 64, 64, 128));
+      for (int g = 0; g < groups; ++g) {
+        tj::PolyParams pg = pp;
+        pg.bh0 = g * G;
+        const int n = std::min(G, BH - pg.bh0);
+        if (n <= 0) break;
+        TJ_CHECK(timed_launch(m, TJ_K_POLY, 1, st, [&]() -> int {
+          tj::poly_update_kernel<<<dim3(tj::kPolyFeatBlocks, n), 192, tj::kUpdSmem, st>>>(tkt, tv, pg);
+          TJ_CUDA(cudaGetLastError());
+          return TJ_OK;
+        }));
+        TJ_CUDA(cudaEventRecord(cm->events[2 * g], st));
+        TJ_CUDA(cudaStreamWaitEvent(cm->side, cm->events[2 * g], 0));
+        float* gath = w.gathered + (size_t)pg.bh0 * per * world;
+        TJ_CHECK(nccl_check(cm, nc.AllGather(w.total + (size_t)pg.bh0 * per, gath, (size_t)n * per, ncclFloat32,
+                                             cm->comm, cm->side), "state all-gather"));
+        if (rank > 0) {
+          tj::poly_fixup_kernel<<<1184, 256, 0, cm->side>>>(gath, rank, n, pg.bh0, w.snap,
+                                                            n_chunks - pp.prefix_chunks, pp.prefix_chunks,
+                                                            pp.t_before);
+          TJ_CUDA(cudaGetLastError());
+        }
+        TJ_CUDA(cudaEventRecord(cm->events[2 * g + 1], cm->side));
+      }
+      for (int g = 0; g < groups; ++g) {
+        tj::PolyParams pg = pp;
+        pg.bh0 = g * G;
+        const int n = std::min(G, BH - pg.bh0);
+        if (n <= 0) break;
+        TJ_CUDA(cudaStreamWaitEvent(st, cm->events[2 * g + 1], 0));
+        TJ_CHECK(timed_launch(m, TJ_K_POLY, 1, st, [&]() -> int {
+          tj::poly_apply_kernel<<<dim3((n_chunks - pp.prefix_chunks) * 4, n), tj::kAppThreads, tj::kAppSmem, st>>>(
+              tq, tk, tv, tsn, pg);
+          TJ_CUDA(cudaGetLastError());
+          return TJ_OK;
+        }));
+      }
       if (rank == 0) {  // exact prefix: every key it needs is local
         tj::AttnParams ap = ap0;
         ap.poly_admit = &w.ctl->admit;
@@ -1232,6 +1283,8 @@ int tj_comm_create(const void* id, int rank, int world, int timeout_ms, TjComm**
 
 int tj_comm_destroy(TjComm* c) {
   if (!c) return TJ_OK;
+  for (cudaEvent_t e : c->events) cudaEventDestroy(e);
+  if (c->side) cudaStreamDestroy(c->side);
   if (c->comm) {
     if (c->broken) tj::nccl().CommAbort(c->comm);
     else tj::nccl().CommDestroy(c->comm);

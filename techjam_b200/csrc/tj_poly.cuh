@@ -78,6 +78,9 @@ struct PolyParams {
   float* total;
   int all_chunks;
   int guard_shards;  // shards whose guard samples were pooled (all-reduced) before finalize
+  // The update and apply kernels cover heads bh0 .. bh0 + gridDim.y - 1 of
+  // the B*H (batch, head) pairs (0 for a launch over all of them).
+  int bh0;
 };
 
 // ------------------------------------------------------------------ guard
@@ -284,7 +287,7 @@ __global__ void __launch_bounds__(192, 1)
                        const PolyParams p) {
   if (p.ctl->admit == 0 || error_raised(p.err)) return;
   const int fb = blockIdx.x;
-  const int bh = blockIdx.y;
+  const int bh = p.bh0 + (int)blockIdx.y;
   const int n_chunks = p.S / kPolyChunk;
   // the last chunk's keys feed no later query of this shard (only later shards)
   const int n_sub = (p.all_chunks ? n_chunks : n_chunks - 1) * 4;
@@ -442,7 +445,7 @@ __global__ void __launch_bounds__(kAppThreads, 1)
                       const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmSnap,
                       const PolyParams p) {
   if (p.ctl->admit == 0 || error_raised(p.err)) return;
-  const int bh = blockIdx.y;
+  const int bh = p.bh0 + (int)blockIdx.y;
   const int b = bh / p.H, h = bh - (bh / p.H) * p.H;
   const int n_chunks = p.S / kPolyChunk;
   const int u = p.prefix_chunks * 4 + (int)blockIdx.x;  // global 128-query block
@@ -702,9 +705,11 @@ __global__ void __launch_bounds__(kAppThreads, 1)
 // snapshots.  gathered = every shard's total state [world][B*H][80][4224]
 // fp32; local snapshot c holds the mean over this shard's first 512c tokens;
 // afterwards it holds the mean over all tokens before its chunk.
+// Heads bh0 .. bh0 + BH - 1; gathered = every shard's total of those heads,
+// [world][BH][80][4224].
 __global__ void __launch_bounds__(256) poly_fixup_kernel(const float* __restrict__ gathered, int rank, int BH,
-                                                          __half* __restrict__ snap, int n_snap, int prefix_chunks,
-                                                          float t_before) {
+                                                          int bh0, __half* __restrict__ snap, int n_snap,
+                                                          int prefix_chunks, float t_before) {
   // Eight consecutive state elements per thread: the earlier shards' sum is
   // formed once (two float4 loads per shard), then every snapshot of those
   // elements is rewritten with one 16-byte load and store.  Memory-bound:
@@ -721,7 +726,7 @@ __global__ void __launch_bounds__(256) poly_fixup_kernel(const float* __restrict
       before[0] += a.x; before[1] += a.y; before[2] += a.z; before[3] += a.w;
       before[4] += b.x; before[5] += b.y; before[6] += b.z; before[7] += b.w;
     }
-    const size_t bh = e / per, rem = e - bh * per;
+    const size_t bh = bh0 + e / per, rem = e - (e / per) * per;
     uint4* sp = reinterpret_cast<uint4*>(snap + bh * n_snap * per + rem);
 #pragma unroll 4
     for (int i = 0; i < n_snap; ++i) {
