@@ -154,6 +154,14 @@ TJ_API int tj_set_wait_limit(unsigned long long ns);
    or hangs; the context stays usable. */
 TJ_API int tj_wait_selftest(TjModel* model, int* err, void* stream);
 
+/* Programmatic dependent launch in tj_forward (no counterpart in the
+   reference): -1 = by size (on for batch*seq_len*d_model <= 2^24, where
+   kernels are short enough that overlapping each one's launch and prologue
+   with its predecessor's tail pays), 0 = never, 1 = always.  The initial
+   mode is TJ_PDL from the environment (unset: -1).  Process-wide; changes
+   no result bit. */
+TJ_API int tj_set_pdl(int mode);
+
 /* ---- per-kernel timing (CUDA events recorded around each launch) ------- */
 
 typedef enum TjKernelClass {

@@ -58,6 +58,7 @@ SIGNATURES = {
     "tj_forward_noalloc": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]),
     "tj_device_error": (c_int, [c_void_p, POINTER(c_int)]),
     "tj_set_wait_limit": (c_int, [ctypes.c_ulonglong]),
+    "tj_set_pdl": (c_int, [c_int]),
     "tj_wait_selftest": (c_int, [c_void_p, c_void_p, c_void_p]),
     "tj_profile_begin": (c_int, [c_void_p, c_int]),
     "tj_profile_end": (c_int, [c_void_p, POINTER(ctypes.c_double), POINTER(ctypes.c_longlong)]),

@@ -112,6 +112,8 @@ __global__ void __launch_bounds__(AttnCfg<HD>::kThreads, 1)
                     const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
   using Cfg = AttnCfg<HD>;
   constexpr int ST = Cfg::kStages;
+  griddep_launch_dependents();
+  griddep_wait();  // Q/K/V and lengths come from earlier kernels
   const int bh = blockIdx.y;
   const int b = bh / p.H;
   const int h = bh - b * p.H;
@@ -444,10 +446,6 @@ __global__ void __launch_bounds__(384, 1)
   constexpr int ST = PC::kStages;
   constexpr int NI = PC::kItemSlots;
   const int BH = p.B * p.H;
-  const bool gated = p.poly_admit != nullptr && *reinterpret_cast<const volatile int*>(p.poly_admit) != 0;
-  // an admitted polynomial route leaves only the exact prefix's pairs here
-  const int np = gated ? min(n_pairs, p.exact_pairs) : n_pairs;
-  const int n_items = np * BH;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -493,6 +491,11 @@ __global__ void __launch_bounds__(384, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  griddep_wait();  // Q/K/V, lengths and the scheduler words come from earlier kernels
+  const bool gated = p.poly_admit != nullptr && *reinterpret_cast<const volatile int*>(p.poly_admit) != 0;
+  // an admitted polynomial route leaves only the exact prefix's pairs here
+  const int np = gated ? min(n_pairs, p.exact_pairs) : n_pairs;
+  const int n_items = np * BH;
 
   // Work item decode, identical in every role.
   struct Item {
@@ -560,6 +563,9 @@ __global__ void __launch_bounds__(384, 1)
             pending = claim();
             if (decode(c, it)) { item = c; break; }
           }
+          // nothing left to claim: this is the CTA's last item, so the next
+          // kernel may launch and run its prologue while it finishes
+          if (pending >= n_items) griddep_launch_dependents();
           const int slot = n % NI;
           if (n >= NI && !mbar_wait(item_empty + slot, ((n / NI) - 1) & 1, p.err, kErrAttnProducer)) break;
           item_slot[slot] = item;

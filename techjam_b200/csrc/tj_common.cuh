@@ -123,6 +123,16 @@ TJ_DEV void tmem_dealloc(uint32_t taddr, uint32_t ncols) {  // whole warp
   asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
 }
 TJ_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+
+// Programmatic dependent launch (kernels launched with programmatic stream
+// serialisation): griddep_launch_dependents lets the next kernel of the
+// stream launch now, so its CTAs take SMs as this kernel's CTAs retire and run
+// their prologue (barriers, TMEM, descriptor prefetch) meanwhile;
+// griddep_wait blocks until the kernels this one depends on have completed
+// and their memory is visible -- every kernel calls it before it reads
+// anything an earlier kernel wrote.  Both are no-ops for a plain launch.
+TJ_DEV void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+TJ_DEV void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 TJ_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
 // Per-warpgroup register budget (every warp of a warpgroup executes the same

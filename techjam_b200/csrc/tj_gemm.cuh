@@ -339,6 +339,7 @@ __global__ void __launch_bounds__(320, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  griddep_wait();  // operands, tile list and residual come from earlier kernels
 
   const int n_tiles = (p.N + BN - 1) / BN;
   const int total = __ldg(p.n_live) * n_tiles;
@@ -364,6 +365,9 @@ __global__ void __launch_bounds__(320, 1)
         if (++stage == S) { stage = 0; phase ^= 1u; }
       }
     }
+    // every load of this CTA is issued: the next kernel may launch and run
+    // its prologue while the last tiles drain
+    griddep_launch_dependents();
   } else if (warp == 1) {  // whole warp; tcgen05 issues from the elected lane
     // ------------------------------------------------------------ MMA issuer
     constexpr uint32_t idesc = idesc_f16_f32(kGemmBM, BN, false, false);
@@ -483,6 +487,7 @@ __global__ void __launch_bounds__(320, 1)
   cluster_sync();  // both CTAs' barriers exist before any remote arrive or multicast commit
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  griddep_wait();  // operands, tile list and residual come from earlier kernels
 
   const int n_live = __ldg(p.n_live);
   const int n_tiles = p.N / BN;
@@ -517,6 +522,7 @@ __global__ void __launch_bounds__(320, 1)
         if (++stage == S) { stage = 0; phase ^= 1u; }
       }
     }
+    griddep_launch_dependents();  // every load of this CTA is issued
   } else if (warp == 1 && rank == 0) {  // whole warp; tcgen05 issues from the elected lane
     // ------------------------------------------------------------ 2-SM MMA issuer (even CTA)
     constexpr uint32_t idesc = idesc_f16_f32(256, BN, false, false);

@@ -17,6 +17,8 @@ __global__ void __launch_bounds__(1024) prep_lengths_kernel(const uint8_t* __res
                                                              uint8_t* __restrict__ general, int* __restrict__ sched,
                                                              int* __restrict__ counts) {
   const int b = blockIdx.x;
+  griddep_launch_dependents();
+  griddep_wait();
   if (sched != nullptr && b == 0 && threadIdx.x < 2) sched[threadIdx.x] = 0;
   if (mask == nullptr) {
     if (threadIdx.x == 0) {
@@ -74,6 +76,8 @@ __global__ void __launch_bounds__(1024) prep_lengths_kernel(const uint8_t* __res
 // least one row inside its sample's valid prefix.  One block of 1024 threads.
 __global__ void prep_tiles_kernel(const int* __restrict__ lengths, int B, int S, int* __restrict__ tile_list,
                                   int* __restrict__ n_live, uint8_t* __restrict__ tile_live) {
+  griddep_launch_dependents();
+  griddep_wait();
   const long long M = (long long)B * S;
   const int n_tiles = (int)((M + kTileRows - 1) / kTileRows);
   __shared__ int s_warp[32];
@@ -130,6 +134,8 @@ __global__ void __launch_bounds__(1024) prep_pack_kernel(const uint8_t* __restri
                                                           const int* __restrict__ counts, int* __restrict__ pack_of,
                                                           int* __restrict__ row_of) {
   const int b = blockIdx.x;
+  griddep_launch_dependents();
+  griddep_wait();
   __shared__ int s_warp[32];
   __shared__ int s_off, s_base;
   // exclusive prefix of the earlier samples' token counts
@@ -193,6 +199,8 @@ __global__ void __launch_bounds__(1024) prep_pack_kernel(const uint8_t* __restri
 __global__ void prep_pack_tiles_kernel(const int* __restrict__ counts, int B, int* __restrict__ row_of,
                                        int* __restrict__ tile_list, int* __restrict__ n_live,
                                        uint8_t* __restrict__ tile_live, int n_tiles_all) {
+  griddep_launch_dependents();
+  griddep_wait();
   __shared__ int s_warp[32];
   int part = 0;
   for (int i = threadIdx.x; i < B; i += blockDim.x) part += counts[i];
@@ -236,6 +244,8 @@ __global__ void __launch_bounds__(256) layernorm_kernel(const float* __restrict_
                                                         const float* __restrict__ beta, void* __restrict__ out,
                                                         int d, float eps, RowValidity valid,
                                                         const uint8_t* __restrict__ tile_live) {
+  griddep_launch_dependents();
+  griddep_wait();
   const long long row = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= valid.M) return;

@@ -235,3 +235,30 @@ def test_varlen_packing_is_exact():
             assert torch.equal(full[b, :n], alone[0]), f"sample {b} (length {n}) differs from its solo run"
         assert torch.equal(cand(x, torch.ones_like(mask)), cand(x, None))
         assert cand.device_error() == 0
+
+
+@pytest.mark.parametrize("shape", [(2, 2048, 1024, 16, 4096, 2, 0.5), (32, 256, 512, 8, 2048, 2, 0.75)])
+def test_dependent_launch_changes_no_bit(shape):
+    """Programmatic dependent launch only moves each kernel's launch and
+    prologue under its predecessor's tail (every kernel waits for its
+    predecessor before touching shared memory), so forcing it on and off gives
+    bit-identical outputs -- C2's and C3's per-GPU shapes at 8 GPUs, where the
+    size rule turns it on -- and both pass the oracle."""
+    from techjam_b200 import _lib
+    b, n, d, h, f, L, pr = shape
+    cfg = EncoderShape(b, n, d, h, f, L, True)
+    oracle, cand = _models(cfg, 1.0)
+    x, mask = generate_random_case(cfg, DEV, torch.float32, 33, pr)
+    try:
+        outs = []
+        for mode in (1, 0, 1):
+            _lib.call("tj_set_pdl", mode)
+            with torch.inference_mode():
+                outs.append(cand(x, mask).clone())
+            torch.cuda.synchronize(DEV)
+            assert cand.device_error() == 0
+    finally:
+        _lib.call("tj_set_pdl", -1)
+    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[0], outs[2])
+    with torch.inference_mode():
+        _assert_pass(oracle(x, mask), outs[0], mask, cand)
