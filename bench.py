@@ -50,7 +50,7 @@ from techjam_b200 import _lib  # noqa: E402
 from techjam_b200.dispatcher import DispatchingTransformer  # noqa: E402
 from techjam_b200.harness import CONFIGS, generate_random_case, seeded_model, valid_lengths, work  # noqa: E402
 from techjam_b200.sharding import (SeqShardComm, forward_seqshard, gather_batch_outputs, sample_owners,  # noqa: E402
-                                   shard_samples, token_range)
+                                   shard_samples, take_tokens, token_ranges)
 
 SEED = 1234 + 100000  # the reference harness's timing input seed (torch_transformer_benchmark.py:459-466)
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
@@ -74,6 +74,8 @@ def parse_args():
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="C2")
     ap.add_argument("--route", choices=("exact", "poly", "auto"), default="auto")
+    ap.add_argument("--layout", choices=("auto", "contiguous", "zigzag"), default="auto",
+                    help="sequence-shard token layout (auto: zig-zag for the exact route, else contiguous)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-repeats", type=int, default=2)
@@ -257,7 +259,7 @@ def run_reference(args):
     return 0
 
 
-def kernel_rates(cfg, lengths, my_lengths, kms_l, kcnt, steps, world, poly_prefix_here=True):
+def kernel_rates(cfg, lengths, my_lengths, kms_l, kcnt, steps, world, poly_prefix_here=True, seqshard=False):
     """Per-kernel-class rates of one timed pass.
 
     ``kms_l``: ms per step of each libtj kernel class (max over ranks),
@@ -267,7 +269,9 @@ def kernel_rates(cfg, lengths, my_lengths, kms_l, kcnt, steps, world, poly_prefi
     work: the flash kernel, plus the polynomial route's feature GEMMs when it
     ran) and, with the polynomial route, the exact-equivalent attention rate
     (exact causal flops of the whole job / time / GPUs), which the tensor peak
-    does not bound.
+    does not bound.  Sequence-sharded exact attention counts each GPU's
+    share of the whole job's causal flops (its queries attend to every
+    earlier global key, not only its own).
     """
     names = _lib.KERNEL_CLASSES
     w_all = work(cfg, lengths)
@@ -276,6 +280,8 @@ def kernel_rates(cfg, lengths, my_lengths, kms_l, kcnt, steps, world, poly_prefi
                 "gemm_ffn_in": w_mine["gemm_ffn_in_flops"], "gemm_ffn_out": w_mine["gemm_ffn_out_flops"],
                 "attention": w_mine["attn_flops"]}
     poly_i, attn_i = names.index("poly"), names.index("attention")
+    if seqshard:
+        flops_of["attention"] = w_all["attn_flops"] / world
     if kcnt[poly_i]:
         # polynomial route ran: the flash kernel only covered the 4096-token exact prefix, and the
         # poly kernels issue 2*4224*80 tensor flops per key (update) and per query (apply)
@@ -424,14 +430,17 @@ def main():
     comm = None
     if seqshard:
         comm = SeqShardComm(dev)
-        rng = token_range(cfg.seq_len, world, rank)
-        x = x_full[:, rng.start:rng.stop].contiguous()
+        # the exact route's causal work grows with position: zig-zag chunks
+        # balance it; the polynomial route's work is linear, so contiguous
+        layout = args.layout if args.layout != "auto" else ("zigzag" if args.route == "exact" else "contiguous")
+        rngs = token_ranges(cfg.seq_len, world, rank, layout)
+        x = take_tokens(x_full, rngs)
         mask = None
-        my_lengths = [len(rng)] * cfg.batch_size
-        parallelism = f"sequence-shard x{world} (NCCL state/KV exchange)"
+        my_lengths = [x.shape[1]] * cfg.batch_size
+        parallelism = f"sequence-shard x{world} ({layout}; NCCL state/KV exchange)"
 
         def fwd(inp, msk):
-            return forward_seqshard(model, comm, inp, args.route)
+            return forward_seqshard(model, comm, inp, args.route, layout)
     else:
         if cfg.batch_size < world:
             raise SystemExit(f"{wl.name} has {cfg.batch_size} samples: batch sharding needs at least one per GPU "
@@ -551,7 +560,7 @@ def main():
     # the kernels run for microseconds inside a few-millisecond step: burst figure
     peak = peaks["bf16_tflops"]
     rates = kernel_rates(cfg, lengths, my_lengths, kms_l, list(kcnt), args.steps, world,
-                         poly_prefix_here=(not seqshard or rank == 0))
+                         poly_prefix_here=(not seqshard or rank == 0), seqshard=seqshard)
     kernels, dom = rates["kernels"], rates["dominant"]
     achieved, attn_tflops, attn_exact_eq = rates["achieved"], rates["attn_tflops"], rates["attn_exact_eq"]
     w_all = work(cfg, lengths)

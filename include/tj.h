@@ -60,6 +60,14 @@ typedef enum TjAttentionRoute {
   TJ_ROUTE_AUTO = 2   /* poly for long causal unpadded sequences, exact otherwise */
 } TjAttentionRoute;
 
+/* Which tokens a rank holds under sequence sharding (P ranks, sequence S). */
+typedef enum TjShardLayout {
+  TJ_SHARD_CONTIGUOUS = 0, /* rank r: [r*S/P, (r+1)*S/P) */
+  TJ_SHARD_ZIGZAG = 1      /* rank r: chunks r and 2P-1-r of S/(2P) tokens, back to
+                              back -- every rank gets the same causal attention
+                              work; exact route only */
+} TjShardLayout;
+
 typedef struct TjConfig {
   int d_model;
   int num_heads;
@@ -241,9 +249,12 @@ TJ_API int tj_comm_create(const void* id, int rank, int world, int timeout_ms, T
 TJ_API int tj_comm_destroy(TjComm* comm);
 TJ_API int tj_workspace_bytes_seqshard(const TjModel* model, const TjComm* comm, int batch, int seq_local, int route,
                                        size_t* bytes);
-/* Forward of rank r's sequence shard: x/out hold global tokens
-   [r*seq_local, (r+1)*seq_local) of every sample ([B, seq_local, d], FP32),
-   causal, no padding.  Token-local work runs on the shard; attention takes
+/* Forward of rank r's sequence shard: x/out hold rank r's tokens of every
+   sample ([B, seq_local, d], FP32, causal, no padding) -- global tokens
+   [r*seq_local, (r+1)*seq_local) for TJ_SHARD_CONTIGUOUS, or the chunks
+   [r*h, (r+1)*h) and [(2P-1-r)*h, (2P-r)*h), h = seq_local/2, in that order
+   for TJ_SHARD_ZIGZAG (route TJ_ROUTE_EXACT only, seq_local a multiple of
+   512).  Token-local work runs on the shard; attention takes
    the guarded polynomial route (guard statistics all-reduced so every rank
    decides alike; each rank's state total all-gathered and folded into its
    snapshots) or the exact flash route over all-gathered K/V.  The guard runs
@@ -256,7 +267,7 @@ TJ_API int tj_workspace_bytes_seqshard(const TjModel* model, const TjComm* comm,
    prefix streaming of forward_prefix_chunks
    (src/implementations/extreme.py:167-204). */
 TJ_API int tj_forward_seqshard(TjModel* model, TjComm* comm, const float* x, float* out, int batch, int seq_local,
-                               int route, void* workspace, size_t workspace_bytes, void* stream);
+                               int route, int layout, void* workspace, size_t workspace_bytes, void* stream);
 /* The sequence-sharded guard's cached verdict for a layer: 1 polynomial
    route, 0 exact route, -1 not evaluated yet (no counterpart in the
    reference beyond PolyOrFlashSelfAttention.route_name, extreme.py:268-272). */

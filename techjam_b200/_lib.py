@@ -76,8 +76,8 @@ SIGNATURES = {
     "tj_comm_destroy": (c_int, [c_void_p]),
     "tj_workspace_bytes_seqshard": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, POINTER(c_size_t)]),
     "tj_seqshard_route": (c_int, [c_void_p, c_int, POINTER(c_int)]),
-    "tj_forward_seqshard": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_size_t,
-                                    c_void_p]),
+    "tj_forward_seqshard": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p,
+                                    c_size_t, c_void_p]),
     "tj_poly_workspace_bytes": (c_int, [c_int, c_int, c_int, c_int, POINTER(c_size_t)]),
     "tj_poly_attention_f16": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int,
                                       c_void_p, c_size_t, c_void_p, c_void_p]),

@@ -1156,7 +1156,7 @@ __global__ void fill_int_kernel(int* dst, int n, int value) {
 
 // Attention of one layer on a sequence shard: guarded polynomial route with a
 // state exchange, or exact flash over all-gathered K/V.
-int shard_attention(TjModel* m, TjComm* cm, ShardWorkspace& w, int layer, int B, int S_loc, int route,
+int shard_attention(TjModel* m, TjComm* cm, ShardWorkspace& w, int layer, int B, int S_loc, int route, int layout,
                     const tj::AttnParams& ap0, cudaStream_t st) {
   const TjConfig& c = m->cfg;
   const int H = c.num_heads, hd = c.d_model / H, d = c.d_model;
@@ -1293,9 +1293,15 @@ int shard_attention(TjModel* m, TjComm* cm, ShardWorkspace& w, int layer, int B,
   TJ_CHECK(nccl_check(cm, nc.AllGather(w.base.v, w.vg, kv, ncclFloat16, cm->comm, st), "V all-gather"));
   tj::AttnParams ap = ap0;
   ap.poly_admit = nullptr;
-  ap.q_pos0 = rank * S_loc;
   ap.kv_shard = S_loc;
   ap.kv_shards = world;
+  if (layout == TJ_SHARD_ZIGZAG) {  // chunks rank and 2*world-1-rank of S_loc/2 tokens
+    ap.zz_chunk = S_loc / 2;
+    ap.q_pos0 = rank * ap.zz_chunk;
+    ap.q_pos1 = (2 * world - 1 - rank) * ap.zz_chunk;
+  } else {
+    ap.q_pos0 = rank * S_loc;
+  }
   return timed_launch(m, TJ_K_ATTN, 1, st, [&] { return launch_attention(w.base.q, w.kg, w.vg, hd, ap, B, st); });
 }
 
@@ -1364,13 +1370,18 @@ int tj_workspace_bytes_seqshard(const TjModel* m, const TjComm* c, int B, int S_
   return TJ_OK;
 }
 
-int tj_forward_seqshard(TjModel* m, TjComm* cm, const float* x, float* out, int B, int S_loc, int route, void* ws,
-                        size_t ws_bytes, void* stream) {
+int tj_forward_seqshard(TjModel* m, TjComm* cm, const float* x, float* out, int B, int S_loc, int route, int layout,
+                        void* ws, size_t ws_bytes, void* stream) {
   if (!m || !cm || !x || !out || !ws) return fail(TJ_ERR_INVALID, "null argument");
   if (cm->broken || !cm->comm) return fail(TJ_ERR_NCCL, "communicator is broken");
   if (B <= 0 || S_loc <= 0 || S_loc % 128) return fail(TJ_ERR_UNSUPPORTED, "seq_len per shard must be a multiple of 128");
   if (x == out) return fail(TJ_ERR_INVALID, "x and out must not alias");
   if (!m->cfg.causal) return fail(TJ_ERR_UNSUPPORTED, "sequence sharding needs causal attention");
+  if (layout != TJ_SHARD_CONTIGUOUS && layout != TJ_SHARD_ZIGZAG) return fail(TJ_ERR_INVALID, "unknown layout %d", layout);
+  if (layout == TJ_SHARD_ZIGZAG && route != TJ_ROUTE_EXACT)
+    return fail(TJ_ERR_UNSUPPORTED, "the zig-zag layout balances the exact route; pass TJ_ROUTE_EXACT");
+  if (layout == TJ_SHARD_ZIGZAG && S_loc % 512 != 0)
+    return fail(TJ_ERR_UNSUPPORTED, "zig-zag sharding needs seq_local a multiple of 512 (two 256-aligned chunks)");
   const TjConfig& c = m->cfg;
   const size_t need = carve_shard(c, B, S_loc, cm->world, route, nullptr, nullptr);
   if (ws_bytes < need) return fail(TJ_ERR_INVALID, "workspace %zu bytes < required %zu", ws_bytes, need);
@@ -1414,7 +1425,7 @@ int tj_forward_seqshard(TjModel* m, TjComm* cm, const float* x, float* out, int 
     }));
     gp.N = 3 * d; gp.K = d; gp.bias = L.bqkv;
     TJ_CHECK(timed_launch(m, TJ_K_QKV, 1, st, [&] { return launch_gemm_epi(tj::kEpiQKV, w.base.act, L.wqkv, gp, di.sms, st); }));
-    TJ_CHECK(shard_attention(m, cm, w, l, B, S_loc, route, ap, st));
+    TJ_CHECK(shard_attention(m, cm, w, l, B, S_loc, route, layout, ap, st));
     gp.N = d; gp.K = d; gp.bias = L.bo; gp.out32 = out; gp.resid = resid_in;
     TJ_CHECK(timed_launch(m, TJ_K_OUT, 1, st, [&] { return launch_gemm_epi(tj::kEpiResid, w.base.act, L.wo, gp, di.sms, st); }));
     TJ_CHECK(timed_launch(m, TJ_K_LN, 1, st, [&] {

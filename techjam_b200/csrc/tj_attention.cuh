@@ -47,9 +47,16 @@ struct AttnParams {
   // K/V hold kv_shard rows per (shard, b, h): the key at global position pos
   // is row ((pos / kv_shard * B + b) * H + h) * kv_shard + pos % kv_shard.
   // Unsharded: q_pos0 = 0, kv_shard = S.
+  // Zig-zag sharding (zz_chunk > 0, a multiple of 256): the sequence is cut
+  // into 2 * kv_shards chunks of zz_chunk tokens and shard r holds chunks r
+  // and 2 * kv_shards - 1 - r back to back (kv_shard = 2 * zz_chunk), so
+  // every shard gets the same causal work; local query row zz_chunk sits at
+  // global position q_pos1.
   int q_pos0;
   int kv_shard;
   int kv_shards;  // shards present in K/V (1 unless sharded)
+  int zz_chunk;
+  int q_pos1;
   int B;
   // Persistent kernel's work scheduler: {next item, CTAs finished}, zero
   // before the launch and zero again after it (the last CTA to finish resets
@@ -59,6 +66,28 @@ struct AttnParams {
   // (-1: padding, not written).  Null: row b*S + n.
   const int* pack_of;
 };
+
+// Global 128-token tile of local query tile q (a tile never straddles a
+// zig-zag chunk: zz_chunk is a multiple of 256, so neither does a pair).
+TJ_DEV int q_global_tile(const AttnParams& p, int q) {
+  const int r = q * 128;
+  if (p.zz_chunk == 0 || r < p.zz_chunk) return (p.q_pos0 + r) / 128;
+  return (p.q_pos1 + r - p.zz_chunk) / 128;
+}
+// First K/V row of the 128-key tile that starts at global position pos.
+TJ_DEV int kv_tile_row(const AttnParams& p, int b, int h, int pos) {
+  int shard, off;
+  if (p.zz_chunk > 0) {
+    const int c = pos / p.zz_chunk;
+    const bool first = c < p.kv_shards;
+    shard = first ? c : 2 * p.kv_shards - 1 - c;
+    off = (first ? 0 : p.zz_chunk) + (pos - c * p.zz_chunk);
+  } else {
+    shard = pos / p.kv_shard;
+    off = pos - shard * p.kv_shard;
+  }
+  return ((shard * p.B + b) * p.H + h) * p.kv_shard + off;
+}
 
 // Context row of query token (b, qrow), or -1 when it is not written.
 TJ_DEV long long ctx_row(const AttnParams& p, int b, int qrow) {
@@ -121,7 +150,7 @@ __global__ void __launch_bounds__(AttnCfg<HD>::kThreads, 1)
   const int pair = p.causal ? (n_pairs - 1 - (int)blockIdx.x) : (int)blockIdx.x;
   const int len = __ldg(p.lengths + b);  // valid keys (global positions)
   const int q0 = 2 * pair;               // local query tile of warpgroup 0
-  const int qg0 = p.q_pos0 / 128 + q0;   // its global tile
+  const int qg0 = q_global_tile(p, q0);  // its global tile
   if (qg0 * 128 >= len || q0 * 128 >= p.S) return;
   if (error_raised(p.err)) return;
   if (p.poly_admit != nullptr && pair >= p.exact_pairs && *reinterpret_cast<const volatile int*>(p.poly_admit) != 0)
@@ -171,11 +200,7 @@ __global__ void __launch_bounds__(AttnCfg<HD>::kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const int row0 = bh * p.S;  // first Q row of this (b, h) in the [B*H*S, HD] view
-  auto kv_row = [&](int j) {  // first K/V row of key tile j (global positions j*128 ..)
-    const int pos = j * 128;
-    const int shard = pos / p.kv_shard;
-    return ((shard * p.B + b) * p.H + h) * p.kv_shard + (pos - shard * p.kv_shard);
-  };
+  auto kv_row = [&](int j) { return kv_tile_row(p, b, h, j * 128); };  // key tile j (global positions j*128 ..)
 
   if (warp == 8) {
     if (lane == 0) {
@@ -509,7 +534,7 @@ __global__ void __launch_bounds__(384, 1)
     it.h = it.bh - it.b * p.H;
     it.len = __ldg(p.lengths + it.b);
     it.q0 = 2 * pair;
-    it.qg0 = p.q_pos0 / 128 + it.q0;
+    it.qg0 = q_global_tile(p, it.q0);
     if (it.qg0 * 128 >= it.len || it.q0 * 128 >= p.S) return false;
     it.has1 = (it.qg0 + 1) * 128 < it.len && (it.q0 + 1) * 128 < p.S;
     const int kv_all = (it.len + 127) / 128;
@@ -519,11 +544,7 @@ __global__ void __launch_bounds__(384, 1)
     it.general = p.mask != nullptr && __ldg(p.general + it.b) != 0;
     return true;
   };
-  auto kv_row = [&](const Item& it, int j) {
-    const int pos = j * 128;
-    const int shard = pos / p.kv_shard;
-    return ((shard * p.B + it.b) * p.H + it.h) * p.kv_shard + (pos - shard * p.kv_shard);
-  };
+  auto kv_row = [&](const Item& it, int j) { return kv_tile_row(p, it.b, it.h, j * 128); };
   // Consumer side of the item ring (whole warp): the n-th published item, or
   // -1 once the producer has run out of work.
   auto next_item = [&](int n, int& item, int site) -> bool {

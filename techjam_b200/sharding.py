@@ -11,8 +11,10 @@ batch and prefix chunks through one GPU, src/implementations/extreme.py:136-204)
   ``[B, N, d]`` buffer (NCCL point-to-point).
 * **Sequence sharding** (one long sequence per sample): ``SeqShardComm`` joins
   libtj's own NCCL communicator (the unique id travels over the existing
-  torch.distributed group) and ``forward_seqshard`` runs rank r's token range
-  ``[r*S/P, (r+1)*S/P)``; libtj exchanges the polynomial prefix state (or the
+  torch.distributed group) and ``forward_seqshard`` runs rank r's tokens --
+  the contiguous range ``[r*S/P, (r+1)*S/P)``, or (``layout="zigzag"``, exact
+  route) chunks r and 2P-1-r of S/(2P) tokens, which gives every rank the same
+  causal attention work; libtj exchanges the polynomial prefix state (or the
   K/V shards on the exact route) with NCCL on the compute stream.
 """
 
@@ -110,6 +112,33 @@ def token_range(seq_len: int, world: int, rank: int) -> range:
     return range(rank * per, (rank + 1) * per)
 
 
+_LAYOUTS = {"contiguous": 0, "zigzag": 1}
+
+
+def token_ranges(seq_len: int, world: int, rank: int, layout: str = "contiguous") -> List[range]:
+    """Global token positions held by ``rank``, in local row order: one range
+    (contiguous) or chunks ``rank`` and ``2*world-1-rank`` of ``seq_len/(2*world)``
+    tokens (zig-zag; each chunk a multiple of 256 tokens)."""
+    if layout == "contiguous":
+        return [token_range(seq_len, world, rank)]
+    if layout != "zigzag":
+        raise ValueError(f"unknown layout {layout!r}")
+    if seq_len % (512 * world):
+        raise ValueError(f"zig-zag sharding needs seq_len a multiple of {512 * world} for {world} ranks")
+    h = seq_len // (2 * world)
+    return [range(rank * h, (rank + 1) * h), range((2 * world - 1 - rank) * h, (2 * world - rank) * h)]
+
+
+def take_tokens(x: torch.Tensor, ranges: Sequence[range]) -> torch.Tensor:
+    """The rows of ``x`` ([B, S, ...]) at ``ranges``, in order, contiguous."""
+    return torch.cat([x[:, r.start:r.stop] for r in ranges], dim=1).contiguous()
+
+
+def causal_work(ranges: Sequence[range]) -> int:
+    """Causal attention work of a rank's queries: sum over them of (position + 1)."""
+    return sum((r.start + r.stop + 1) * len(r) // 2 for r in ranges)
+
+
 class SeqShardComm:
     """libtj's NCCL communicator for the ranks of a torch.distributed group."""
 
@@ -146,10 +175,15 @@ class SeqShardComm:
 
 
 def forward_seqshard(model: B200Transformer, comm: SeqShardComm, x_local: torch.Tensor,
-                     route: str = "auto") -> torch.Tensor:
-    """Rank ``comm.rank``'s shard of the forward: ``x_local`` holds its token
-    range of every sample ([B, S/P, d] FP32, causal, no padding); returns the
-    matching output rows."""
+                     route: str = "auto", layout: str = "contiguous") -> torch.Tensor:
+    """Rank ``comm.rank``'s shard of the forward: ``x_local`` holds its tokens
+    of every sample (``token_ranges(S, P, rank, layout)``; [B, S/P, d] FP32,
+    causal, no padding); returns the matching output rows.  The zig-zag
+    layout takes the exact route only."""
+    if layout not in _LAYOUTS:
+        raise ValueError(f"unknown layout {layout!r}")
+    if layout == "zigzag" and route != "exact":
+        raise ValueError("the zig-zag layout balances the exact route; pass route='exact'")
     if x_local.device != comm.device or x_local.dtype != torch.float32 or x_local.ndim != 3:
         raise ValueError("x_local must be FP32 [B, S/P, d] on the communicator's device")
     x_local = x_local.contiguous()
@@ -167,7 +201,8 @@ def forward_seqshard(model: B200Transformer, comm: SeqShardComm, x_local: torch.
     stream = torch.cuda.current_stream(x_local.device)
     with torch.cuda.device(x_local.device):
         _lib.call("tj_forward_seqshard", handle.ptr, comm.ptr, x_local.data_ptr(), out.data_ptr(), batch, s_loc,
-                  _ROUTES[route], ws.data_ptr(), ws.numel(), ctypes.c_void_p(stream.cuda_stream))
+                  _ROUTES[route], _LAYOUTS[layout], ws.data_ptr(), ws.numel(),
+                  ctypes.c_void_p(stream.cuda_stream))
     return out
 
 

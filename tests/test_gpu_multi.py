@@ -26,7 +26,8 @@ def _rank_main(rank, port, results):
     from oracle.reference_model import EncoderShape
     from techjam_b200.dispatcher import DispatchingTransformer
     from techjam_b200.harness import generate_random_case, seeded_model
-    from techjam_b200.sharding import SeqShardComm, forward_seqshard, seqshard_routes, token_range
+    from techjam_b200.sharding import (SeqShardComm, forward_seqshard, seqshard_routes, take_tokens, token_range,
+                                       token_ranges)
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
@@ -49,6 +50,18 @@ def _rank_main(rank, port, results):
                 outs[route] = torch.cat(parts, dim=1).cpu()
                 if route == "exact":
                     assert seqshard_routes(model) == [-1]  # the exact route runs no guard
+            # zig-zag layout on the exact route: rank r holds chunks r and 3-r of 4096 tokens
+            zz = token_ranges(cfg.seq_len, WORLD, rank, "zigzag")
+            y = forward_seqshard(model, comm, take_tokens(x, zz), "exact", "zigzag")
+            parts = [torch.empty_like(y) for _ in range(WORLD)]
+            dist.all_gather(parts, y)
+            full = torch.empty_like(x)
+            for r, part in enumerate(parts):
+                col = 0
+                for rg in token_ranges(cfg.seq_len, WORLD, r, "zigzag"):
+                    full[:, rg.start:rg.stop] = part[:, col:col + len(rg)]
+                    col += len(rg)
+            outs["exact_zigzag"] = full.cpu()
             # the pooled guard admitted the polynomial route (sigma ~0.08 at 0.5x weights) ...
             assert seqshard_routes(model) == [1]
             # ... and a second forward reuses the cached verdict (no guard, no host read) with the same result
@@ -100,6 +113,7 @@ def test_sequence_sharded_forward_two_gpus():
         torch.backends.cuda.matmul.allow_tf32 = old
     # exact route: same kernels, same key tiles in the same order -> identical
     assert torch.equal(outs["exact"], ref_exact)
+    assert torch.equal(outs["exact_zigzag"], ref_exact)
     assert torch.equal(outs["auto_cached"], outs["auto"])
     for route in ("exact", "auto"):
         v = check_outputs(ref, outs[route])

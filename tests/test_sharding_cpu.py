@@ -68,6 +68,30 @@ def test_token_range_rejects_uneven_split():
         token_range(1000, 3, 0)
 
 
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_zigzag_ranges_partition_and_balance_causal_work(world):
+    """Zig-zag: rank r holds chunks r and 2P-1-r; together the ranks cover
+    every token once, and each does exactly 1/P of the causal attention work
+    (the contiguous split gives the last rank (2P-1)/P^2 of it)."""
+    from techjam_b200.sharding import causal_work, take_tokens, token_ranges
+    S = 262144
+    parts = [token_ranges(S, world, r, "zigzag") for r in range(world)]
+    covered = sorted(t for rs in parts for rg in rs for t in (rg.start, rg.stop - 1))
+    assert sorted(p for rs in parts for rg in rs for p in range(rg.start, rg.stop, 4096)) == list(range(0, S, 4096))
+    assert covered[0] == 0 and covered[-1] == S - 1
+    assert all(sum(len(rg) for rg in rs) == S // world for rs in parts)
+    work = [causal_work(rs) for rs in parts]
+    assert len(set(work)) == 1 and sum(work) == S * (S + 1) // 2
+    contiguous = [causal_work(token_ranges(S, world, r)) for r in range(world)]
+    assert max(contiguous) / (sum(contiguous) / world) == pytest.approx((2 * world - 1) / world, rel=1e-4)
+    # local rows are the two chunks back to back
+    x = torch.arange(S).view(1, S, 1)
+    local = take_tokens(x, parts[1]).view(-1).tolist()
+    assert local == list(parts[1][0]) + list(parts[1][1])
+    with pytest.raises(ValueError):
+        token_ranges(S + 512, world, 0, "zigzag")
+
+
 def _gather_main(rank, world, port, results):
     from techjam_b200.sharding import gather_batch_outputs, sample_owners
 
