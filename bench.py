@@ -14,9 +14,10 @@ resident in HBM, CUDA events on the launching stream, barrier + synchronize
 on both sides; for N > 1 including the gather of every rank's output rows
 into rank 0's [B, N, d] buffer, ``value_no_gather`` without it).  ``e2e`` =
 the latency of one call through the public API
-(``DispatchingTransformer.forward``) with the host->device copy of x and the
-mask from pinned memory and the device->host copy of the output inside the
-timed region; ``e2e.pipelined_ms`` = the per-step time when consecutive
+(``DispatchingTransformer.forward``) with the host->device copy of x (the
+valid rows of each right-padded sample, as ``forward_host`` uploads them)
+and the mask from pinned memory and the device->host copy of the whole
+output inside the timed region; ``e2e.pipelined_ms`` = the per-step time when consecutive
 calls overlap their copies.  ``roofline`` = the dominant kernel class,
 measured live with per-launch CUDA events (libtj's profiler) in a second
 pass over the same inputs, against the measured burst peak.
@@ -48,6 +49,7 @@ sys.path.insert(0, str(ROOT))
 
 from techjam_b200 import _lib  # noqa: E402
 from techjam_b200.dispatcher import DispatchingTransformer  # noqa: E402
+from techjam_b200.model import copy_valid_rows, prefix_lengths  # noqa: E402
 from techjam_b200.harness import CONFIGS, generate_random_case, seeded_model, valid_lengths, work  # noqa: E402
 from techjam_b200.sharding import (SeqShardComm, forward_seqshard, gather_batch_outputs, sample_owners,  # noqa: E402
                                    shard_samples, take_tokens, token_ranges)
@@ -324,20 +326,29 @@ def end_to_end(fwd, x, mask, steps, warmup, stream, barrier):
     forward, copy out, one after the other on one stream.  Pipelined: two
     staging slots; the copy-in of step i+1 (own stream) and the copy-out of
     step i-1 (own stream) overlap the forward of step i.  Both time every
-    step's copies on the device with CUDA events.
+    step's copies on the device with CUDA events.  The copy-in is what
+    ``B200Transformer.forward_host`` uploads: each right-padded sample's
+    valid rows (``tj_copy_valid_rows``; the forward never reads padded rows)
+    and the mask; the copy-out is the whole [B, N, d] result.
     """
     dev = x.device
     xh = [x.cpu().pin_memory() for _ in range(2)]
     mh = [None if mask is None else mask.cpu().pin_memory() for _ in range(2)]
     outh = [torch.empty(x.shape, dtype=torch.float32).pin_memory() for _ in range(2)]
     # static device staging: graph replay keeps seeing the same addresses per slot
-    xd = [torch.empty_like(x) for _ in range(2)]
+    xd = [torch.zeros_like(x) for _ in range(2)]  # padded rows are never uploaded: keep them finite
     md = [None if mask is None else torch.empty_like(mask) for _ in range(2)]
-    h2d_bytes = int(x.numel() * 4 + (0 if mask is None else mask.numel()))
+    lengths = prefix_lengths(mh[0], x.shape[0], x.shape[1])
+    row_bytes = x.shape[2] * 4
+    h2d_bytes = int((sum(lengths) * row_bytes if lengths is not None else x.numel() * 4)
+                    + (0 if mask is None else mask.numel()))
     d2h_bytes = int(x.numel() * 4)
 
     def upload(k):
-        xd[k].copy_(xh[k], non_blocking=True)
+        if lengths is not None:
+            copy_valid_rows(xd[k], xh[k], lengths, torch.cuda.current_stream(dev))
+        else:
+            xd[k].copy_(xh[k], non_blocking=True)
         if md[k] is not None:
             md[k].copy_(mh[k], non_blocking=True)
 

@@ -143,6 +143,17 @@ TJ_API int tj_forward(TjModel* model, const float* x, const uint8_t* valid_mask,
 TJ_API int tj_forward_noalloc(TjModel* model, const float* x, const uint8_t* valid_mask, float* out, int batch,
                               int seq_len, int route, void* stream);
 
+/* Host <-> device copy of the valid rows of right-padded samples (no
+   counterpart in the reference, whose inputs start on the device): for each
+   sample b, rows [b*seq_len, b*seq_len + lengths[b]) of row_bytes each, as
+   cudaMemcpyAsync calls on the stream (cudaMemcpyDefault: any direction
+   under unified addressing; pinned host memory for asynchrony), one per run
+   of consecutive rows.  lengths is a host array.  tj_forward never reads
+   the padded rows of x when valid_mask is a right-padded prefix mask, so a
+   caller holding its input in host memory uploads only these rows. */
+TJ_API int tj_copy_valid_rows(void* dst, const void* src, const int* lengths, int batch, int seq_len,
+                              size_t row_bytes, void* stream);
+
 /* Reads (synchronously) and clears the model's device error word: 0 if no
    kernel's bounded wait expired since the last call, else the site code of
    the first wait that did (101-103 GEMM, 201-203 attention, 301 polynomial

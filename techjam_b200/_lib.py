@@ -59,6 +59,7 @@ SIGNATURES = {
     "tj_device_error": (c_int, [c_void_p, POINTER(c_int)]),
     "tj_set_wait_limit": (c_int, [ctypes.c_ulonglong]),
     "tj_set_pdl": (c_int, [c_int]),
+    "tj_copy_valid_rows": (c_int, [c_void_p, c_void_p, POINTER(c_int), c_int, c_int, c_size_t, c_void_p]),
     "tj_wait_selftest": (c_int, [c_void_p, c_void_p, c_void_p]),
     "tj_profile_begin": (c_int, [c_void_p, c_int]),
     "tj_profile_end": (c_int, [c_void_p, POINTER(ctypes.c_double), POINTER(ctypes.c_longlong)]),

@@ -910,6 +910,31 @@ int tj_forward_noalloc(TjModel* m, const float* x, const uint8_t* mask, float* o
   return tj_forward(m, x, mask, out, B, S, route, scratch, need, stream);
 }
 
+int tj_copy_valid_rows(void* dst, const void* src, const int* lengths, int B, int S, size_t row_bytes,
+                       void* stream) {
+  if (!dst || !src || !lengths || B < 0 || S <= 0 || row_bytes == 0) return fail(TJ_ERR_INVALID, "bad arguments");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  auto* d = static_cast<uint8_t*>(dst);
+  const auto* s = static_cast<const uint8_t*>(src);
+  const size_t S_bytes = (size_t)S * row_bytes;
+  size_t run0 = 0, run_len = 0;  // pending run of consecutive rows (bytes)
+  for (int b = 0; b < B; ++b) {
+    const int n = lengths[b];
+    if (n < 0 || n > S) return fail(TJ_ERR_INVALID, "lengths[%d] = %d outside [0, %d]", b, n, S);
+    const size_t start = (size_t)b * S_bytes, bytes = (size_t)n * row_bytes;
+    if (bytes == 0) continue;
+    if (run_len > 0 && run0 + run_len == start) {
+      run_len += bytes;  // previous sample was full: extend the run
+      continue;
+    }
+    if (run_len > 0) TJ_CUDA(cudaMemcpyAsync(d + run0, s + run0, run_len, cudaMemcpyDefault, st));
+    run0 = start;
+    run_len = bytes;
+  }
+  if (run_len > 0) TJ_CUDA(cudaMemcpyAsync(d + run0, s + run0, run_len, cudaMemcpyDefault, st));
+  return TJ_OK;
+}
+
 int tj_poly_workspace_bytes(int B, int H, int S, int exact_prefix, size_t* bytes) {
   if (!bytes || B <= 0 || H <= 0 || S <= 0) return fail(TJ_ERR_INVALID, "bad arguments");
   if (S % tj::kPolyChunk || exact_prefix % tj::kPolyChunk || exact_prefix < tj::kPolyChunk || exact_prefix >= S)

@@ -13,14 +13,15 @@ src/implementations/sdpa.py:96-124, serves the same purpose).
 ``forward(x, valid_token_mask)`` follows the reference's signature and
 semantics (:162-172): FP32 ``[B, N, d]`` in, ``[B, N, d]`` out, padded rows
 exactly 0.  It only accepts CUDA tensors on an sm_100 device: there is no CPU
-path.
+path.  ``forward_host`` takes the same arguments in host memory and uploads
+only the rows the forward reads (each right-padded sample's valid prefix).
 """
 
 from __future__ import annotations
 
 import ctypes
 import weakref
-from typing import Dict, Optional, Tuple
+from typing import Dict, List, Optional, Tuple
 
 import torch
 import torch.nn as nn
@@ -58,6 +59,37 @@ class Block(nn.Module):
 
 
 _ROUTES = {"exact": _lib.ROUTE_EXACT, "poly": _lib.ROUTE_POLY, "auto": _lib.ROUTE_AUTO}
+
+
+def prefix_lengths(mask: Optional[torch.Tensor], batch: int, seq_len: int) -> Optional[List[int]]:
+    """Per-sample valid lengths of a host mask if every row is a right-padded
+    prefix (all rows valid when ``mask`` is None), else None."""
+    if mask is None:
+        return [seq_len] * batch
+    m = mask if mask.dtype == torch.bool else mask != 0
+    lengths = m.sum(1)
+    if not torch.equal(m, torch.arange(seq_len) < lengths[:, None]):
+        return None
+    return [int(n) for n in lengths.tolist()]
+
+
+def copy_valid_rows(dst: torch.Tensor, src: torch.Tensor, lengths: List[int], stream=None) -> int:
+    """Copy rows ``[0, lengths[b])`` of every sample of ``src`` ([B, S, ...],
+    contiguous) into ``dst`` (same shape, either side of the host/device
+    boundary) with ``tj_copy_valid_rows``; returns the bytes copied."""
+    if dst.shape != src.shape or dst.dtype != src.dtype or not (dst.is_contiguous() and src.is_contiguous()):
+        raise ValueError("dst and src must be contiguous tensors of one shape and dtype")
+    batch, seq_len = src.shape[0], src.shape[1]
+    if len(lengths) != batch:
+        raise ValueError("one length per sample")
+    row_bytes = src[0, 0].numel() * src.element_size()
+    dev = dst.device if dst.device.type == "cuda" else src.device
+    stream = stream if stream is not None else torch.cuda.current_stream(dev)
+    arr = (ctypes.c_int * batch)(*lengths)
+    with torch.cuda.device(dev):
+        _lib.call("tj_copy_valid_rows", dst.data_ptr(), src.data_ptr(), arr, batch, seq_len, row_bytes,
+                  ctypes.c_void_p(stream.cuda_stream))
+    return sum(lengths) * row_bytes
 
 
 class _Handle:
@@ -102,6 +134,7 @@ class B200Transformer(nn.Module):
         self.cuda_graphs = False
         self._graphs: Dict[Tuple, Tuple] = {}
         self.graph_kernel_launches = 0  # kernels replayed through graphs (libtj counts host launches only)
+        self._host_stage: Dict[Tuple, Tuple] = {}  # forward_host's device copies of x / mask, per shape
 
     # ---------------------------------------------------------------- packing
     def _param_signature(self, device: torch.device) -> Tuple:
@@ -170,6 +203,7 @@ class B200Transformer(nn.Module):
             self._packed_sig = None
             self._workspaces = {}
             self._graphs = {}
+            self._host_stage = {}
         return result
 
     def enable_cuda_graphs(self, enabled: bool = True) -> "B200Transformer":
@@ -244,6 +278,52 @@ class B200Transformer(nn.Module):
         out = torch.empty((batch, seq_len, self.config.d_model), dtype=torch.float32, device=device)
         launch(out)
         return out if in_dtype == torch.float32 else out.to(in_dtype)
+
+    def forward_host(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor] = None,
+                     out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """``forward`` of host tensors, result in host memory (``out`` if given).
+
+        Uploads only what the forward reads: for a right-padded prefix mask
+        (the reference generator's) each sample's valid rows, else every row;
+        the mask itself; runs ``forward`` on the model's CUDA device (with its
+        CUDA graph when enabled: the device staging buffers are reused per
+        shape) and copies the whole [B, N, d] FP32 result back, padded rows
+        0.  Pinned ``x`` / ``out`` let the copies run asynchronously.  Returns
+        once the result is in host memory.
+        """
+        if x.device.type != "cpu" or x.ndim != 3 or x.shape[-1] != self.config.d_model:
+            raise ValueError(f"x must be a host tensor [B, N, {self.config.d_model}]")
+        batch, seq_len, d = x.shape
+        if valid_token_mask is not None and (valid_token_mask.device.type != "cpu"
+                                             or valid_token_mask.shape != (batch, seq_len)):
+            raise ValueError("valid_token_mask must be a host tensor [B, N]")
+        device = next(self.parameters()).device
+        if device.type != "cuda":
+            raise RuntimeError("move the model to its CUDA device first (there is no CPU path)")
+        xf = x if (x.dtype == torch.float32 and x.is_contiguous()) else x.float().contiguous()
+        key = (batch, seq_len, valid_token_mask is not None)
+        stage = self._host_stage.get(key)
+        if stage is None:
+            # zero-filled once: padded rows that are never uploaded stay finite
+            stage = (torch.zeros((batch, seq_len, d), dtype=torch.float32, device=device),
+                     torch.zeros((batch, seq_len), dtype=torch.bool, device=device)
+                     if valid_token_mask is not None else None)
+            self._host_stage = {key: stage}
+        xd, md = stage
+        lengths = prefix_lengths(valid_token_mask, batch, seq_len)
+        if lengths is not None:
+            copy_valid_rows(xd, xf, lengths)
+        else:
+            xd.copy_(xf, non_blocking=True)
+        if md is not None:
+            m = valid_token_mask if valid_token_mask.dtype == torch.bool else valid_token_mask != 0
+            md.copy_(m, non_blocking=True)
+        y = self.forward(xd, md)
+        if out is None:
+            out = torch.empty((batch, seq_len, d), dtype=torch.float32, pin_memory=True)
+        out.copy_(y, non_blocking=True)
+        torch.cuda.current_stream(device).synchronize()
+        return out if x.dtype == torch.float32 else out.to(x.dtype)
 
     def device_error(self) -> int:
         """Synchronously read and clear the device error word (0 = no expired wait)."""

@@ -262,3 +262,35 @@ def test_dependent_launch_changes_no_bit(shape):
     assert torch.equal(outs[0], outs[1]) and torch.equal(outs[0], outs[2])
     with torch.inference_mode():
         _assert_pass(oracle(x, mask), outs[0], mask, cand)
+
+
+def test_forward_host_uploads_valid_rows_only():
+    """``forward_host`` (host tensors in and out) uploads only each right-padded
+    sample's valid rows; the result equals the device forward bit for bit,
+    padded rows 0, also when a reused ``out`` held a longer sample before,
+    with a non-prefix mask (full upload) and through the CUDA graph."""
+    cfg = EncoderShape(4, 384, 256, 8, 1024, 2, True)
+    oracle, cand = _models(cfg, 1.0)
+    x, mask = generate_random_case(cfg, DEV, torch.float32, 5, 0.5)
+    xh, mh = x.cpu().pin_memory(), mask.cpu()
+    out = torch.full(tuple(x.shape), 7.0).pin_memory()  # stale contents everywhere
+    with torch.inference_mode():
+        ref = cand(x, mask).cpu()
+        got = cand.forward_host(xh, mh, out=out)
+        assert got.data_ptr() == out.data_ptr() and torch.equal(got, ref)
+        # shorter samples into the same host buffer
+        mask2 = mask.clone()
+        mask2[:, 100:] = False
+        ref2 = cand(x, mask2).cpu()
+        assert torch.equal(cand.forward_host(xh, mask2.cpu(), out=out), ref2)
+        assert torch.all(out[~mask2.cpu()] == 0)
+        # a mask with holes: every row is uploaded
+        mask3 = mask.clone()
+        mask3[0, 3] = False
+        assert torch.equal(cand.forward_host(xh, mask3.cpu()), cand(x, mask3).cpu())
+        # CUDA graph replay on the staging buffers
+        cand.enable_cuda_graphs()
+        for _ in range(2):
+            assert torch.equal(cand.forward_host(xh, mh, out=out), ref)
+        cand.enable_cuda_graphs(False)
+        _assert_pass(oracle(x, mask).cpu(), ref, mh, cand)
