@@ -125,7 +125,11 @@ const int g_attn_persist = [] {
 
 // Programmatic dependent launch for the forward-path kernels.  Every kernel
 // launched this way calls griddep_wait before it reads or writes memory that
-// another kernel touches, so it may launch while its predecessor drains (the
+// another kernel touches; griddep_wait tracks only the preceding kernel, so
+// a kernel is launched this way only when that predecessor is one of the
+// forward's own kernels (the first one, after the caller's work, and every
+// launch while the profiler records events between kernels, are ordinary
+// launches).  Such a kernel may launch while its predecessor drains (the
 // GEMMs and the persistent attention signal once their last loads are issued)
 // and run its prologue -- barriers, TMEM allocation, descriptor prefetch --
 // under the predecessor's tail.  That pays where kernels are short: measured
@@ -387,7 +391,14 @@ int launch_layernorm(const float* x, const float* g, const float* b, void* out, 
 // valid tokens and row_of / pack_of map packed rows to padded rows and back.
 int launch_prepare(const uint8_t* mask, int B, int S, int* lengths, uint8_t* general, int* tile_list, int* n_live,
                    uint8_t* tile_live, int* sched, int* counts, int* row_of, int* pack_of, cudaStream_t st) {
-  TJ_CHECK(launch_pdl(tj::prep_lengths_kernel, dim3(B), dim3(1024), 0, st, mask, S, lengths, general, sched, counts));
+  {
+    // The stream's previous work is the caller's (a copy, a memset, an event,
+    // another library's kernel), which griddepcontrol.wait does not track:
+    // the forward's first kernel is an ordinary launch that waits for all of it.
+    const PdlScope first(false);
+    TJ_CHECK(launch_pdl(tj::prep_lengths_kernel, dim3(B), dim3(1024), 0, st, mask, S, lengths, general, sched,
+                        counts));
+  }
   if (row_of != nullptr) {
     TJ_CHECK(launch_pdl(tj::prep_pack_kernel, dim3(B), dim3(1024), 0, st, mask, S, lengths, general, counts, pack_of,
                         row_of));
@@ -772,7 +783,8 @@ int tj_forward(TjModel* m, const float* x, const uint8_t* mask, float* out, int 
   carve(c, B, S, route, static_cast<uint8_t*>(ws), &w);
   const int d = c.d_model, H = c.num_heads, hd = d / H, F = c.ffn_dim;
   const int M = B * S;
-  const PdlScope pdl_scope(pdl_for(M, d));
+  // the profiler's event records sit between the launches: no PDL there
+  const PdlScope pdl_scope(pdl_for(M, d) && !m->prof_on);
 
   // Varlen token packing: with padding present (a mask) the LayerNorm
   // outputs, the GEMMs' fp16 rows and the attention context hold only the

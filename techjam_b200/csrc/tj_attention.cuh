@@ -93,7 +93,7 @@ TJ_DEV int kv_tile_row(const AttnParams& p, int b, int h, int pos) {
 TJ_DEV long long ctx_row(const AttnParams& p, int b, int qrow) {
   if (qrow >= p.S) return -1;
   const long long r = (long long)b * p.S + qrow;
-  return p.pack_of != nullptr ? (long long)__ldg(p.pack_of + r) : r;
+  return p.pack_of != nullptr ? (long long)p.pack_of[r] : r;
 }
 
 template <int HD>
@@ -148,7 +148,7 @@ __global__ void __launch_bounds__(AttnCfg<HD>::kThreads, 1)
   const int h = bh - b * p.H;
   const int n_pairs = gridDim.x;
   const int pair = p.causal ? (n_pairs - 1 - (int)blockIdx.x) : (int)blockIdx.x;
-  const int len = __ldg(p.lengths + b);  // valid keys (global positions)
+  const int len = p.lengths[b];  // valid keys (global positions)
   const int q0 = 2 * pair;               // local query tile of warpgroup 0
   const int qg0 = q_global_tile(p, q0);  // its global tile
   if (qg0 * 128 >= len || q0 * 128 >= p.S) return;
@@ -160,7 +160,7 @@ __global__ void __launch_bounds__(AttnCfg<HD>::kThreads, 1)
   const int nkv0 = p.causal ? qg0 + 1 : kv_all;
   const int nkv1 = has1 ? (p.causal ? qg0 + 2 : kv_all) : 0;
   const int n_kv = nkv0 > nkv1 ? nkv0 : nkv1;
-  const bool general = p.mask != nullptr && __ldg(p.general + b) != 0;
+  const bool general = p.mask != nullptr && p.general[b] != 0;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -532,7 +532,7 @@ __global__ void __launch_bounds__(384, 1)
     it.bh = i % BH;
     it.b = it.bh / p.H;
     it.h = it.bh - it.b * p.H;
-    it.len = __ldg(p.lengths + it.b);
+    it.len = p.lengths[it.b];
     it.q0 = 2 * pair;
     it.qg0 = q_global_tile(p, it.q0);
     if (it.qg0 * 128 >= it.len || it.q0 * 128 >= p.S) return false;
@@ -541,7 +541,7 @@ __global__ void __launch_bounds__(384, 1)
     it.nkv0 = p.causal ? it.qg0 + 1 : kv_all;
     it.nkv1 = it.has1 ? (p.causal ? it.qg0 + 2 : kv_all) : 0;
     it.n_kv = it.nkv0 > it.nkv1 ? it.nkv0 : it.nkv1;
-    it.general = p.mask != nullptr && __ldg(p.general + it.b) != 0;
+    it.general = p.mask != nullptr && p.general[it.b] != 0;
     return true;
   };
   auto kv_row = [&](const Item& it, int j) { return kv_tile_row(p, it.b, it.h, j * 128); };

@@ -131,6 +131,10 @@ TJ_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;
 // griddep_wait blocks until the kernels this one depends on have completed
 // and their memory is visible -- every kernel calls it before it reads
 // anything an earlier kernel wrote.  Both are no-ops for a plain launch.
+// Data an earlier kernel of the same forward wrote is read with plain loads
+// (never __ldg or a const __restrict__ pointer): the compiler may move a
+// non-coherent load, which it takes as invariant for the whole kernel, above
+// the wait.
 TJ_DEV void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 TJ_DEV void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 TJ_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }

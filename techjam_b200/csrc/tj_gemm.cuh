@@ -70,19 +70,19 @@ struct GemmCfg {
 // Padded row of GEMM row `row`, or -1 for a row that holds no valid token.
 TJ_DEV int src_row(const GemmParams& p, int row) {
   if (row >= p.M) return -1;
-  if (p.row_of != nullptr) return __ldg(p.row_of + row);
+  if (p.row_of != nullptr) return p.row_of[row];
   const int b = row / p.seq;
   const int n = row - b * p.seq;
-  if (n >= __ldg(p.lengths + b)) return -1;
+  if (n >= p.lengths[b]) return -1;
   return (p.mask == nullptr || __ldg(p.mask + row) != 0) ? row : -1;
 }
 
 TJ_DEV bool row_is_valid(const GemmParams& p, int row) {
   if (row >= p.M) return false;
-  if (p.row_of != nullptr) return __ldg(p.row_of + row) >= 0;
+  if (p.row_of != nullptr) return p.row_of[row] >= 0;
   const int b = row / p.seq;
   const int n = row - b * p.seq;
-  if (n >= __ldg(p.lengths + b)) return false;
+  if (n >= p.lengths[b]) return false;
   return p.mask == nullptr || __ldg(p.mask + row) != 0;
 }
 
@@ -134,7 +134,7 @@ TJ_DEV bool f16_epilogue(const GemmParams& p, uint32_t taddr, int row0, int colh
       srow[k] = row;
       if (row < p.M) {
         in_m |= 1u << k;
-        if (EPI == kEpiQKV && p.row_of != nullptr) srow[k] = __ldg(p.row_of + row);
+        if (EPI == kEpiQKV && p.row_of != nullptr) srow[k] = p.row_of[row];
       }
     }
   }
@@ -342,7 +342,7 @@ __global__ void __launch_bounds__(320, 1)
   griddep_wait();  // operands, tile list and residual come from earlier kernels
 
   const int n_tiles = (p.N + BN - 1) / BN;
-  const int total = __ldg(p.n_live) * n_tiles;
+  const int total = *p.n_live * n_tiles;
   const int k_blocks = (p.K + kGemmBK - 1) / kGemmBK;
 
   if (warp == 0 && lane == 0) {
@@ -353,7 +353,7 @@ __global__ void __launch_bounds__(320, 1)
     uint32_t phase = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-      const int mt = __ldg(p.tile_list + t / n_tiles);
+      const int mt = p.tile_list[t / n_tiles];
       const int nt = t % n_tiles;
       for (int kb = 0; kb < k_blocks; ++kb) {
         if (!mbar_wait(empty + stage, phase ^ 1u, p.err, kErrGemmProducer)) { ok = false; break; }
@@ -406,7 +406,7 @@ __global__ void __launch_bounds__(320, 1)
     int abuf = 0;
     uint32_t aphase = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
-      const int mt = __ldg(p.tile_list + t / n_tiles);
+      const int mt = p.tile_list[t / n_tiles];
       const int nt = t % n_tiles;
       const int row0 = mt * kGemmBM + quarter * 32;
       const int colh = nt * BN + half * (BN / 2);
@@ -489,7 +489,7 @@ __global__ void __launch_bounds__(320, 1)
   const uint32_t tmem_base = *tmem_slot;
   griddep_wait();  // operands, tile list and residual come from earlier kernels
 
-  const int n_live = __ldg(p.n_live);
+  const int n_live = *p.n_live;
   const int n_tiles = p.N / BN;
   const int total = ((n_live + 1) >> 1) * n_tiles;  // pair tiles
   const int k_blocks = (p.K + kGemmBK - 1) / kGemmBK;
@@ -497,7 +497,7 @@ __global__ void __launch_bounds__(320, 1)
   auto my_mtile = [&](int t, bool& ghost) {
     const int li = 2 * (t / n_tiles) + (int)rank;
     ghost = li >= n_live;
-    return ghost ? (p.M + kGemmBM - 1) / kGemmBM : __ldg(p.tile_list + li);
+    return ghost ? (p.M + kGemmBM - 1) / kGemmBM : p.tile_list[li];
   };
 
   if (warp == 0 && lane == 0) {

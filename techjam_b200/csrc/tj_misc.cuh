@@ -74,7 +74,7 @@ __global__ void __launch_bounds__(1024) prep_lengths_kernel(const uint8_t* __res
 
 // Compact list of 128-row tiles (over the flattened [B*S] rows) holding at
 // least one row inside its sample's valid prefix.  One block of 1024 threads.
-__global__ void prep_tiles_kernel(const int* __restrict__ lengths, int B, int S, int* __restrict__ tile_list,
+__global__ void prep_tiles_kernel(const int* lengths, int B, int S, int* __restrict__ tile_list,
                                   int* __restrict__ n_live, uint8_t* __restrict__ tile_live) {
   griddep_launch_dependents();
   griddep_wait();
@@ -129,9 +129,8 @@ __global__ void prep_tiles_kernel(const int* __restrict__ lengths, int B, int S,
 // A right-padded sample's tokens are its first lengths[b] positions; a
 // general mask's are found with a block-wide scan.
 __global__ void __launch_bounds__(1024) prep_pack_kernel(const uint8_t* __restrict__ mask, int S,
-                                                          const int* __restrict__ lengths,
-                                                          const uint8_t* __restrict__ general,
-                                                          const int* __restrict__ counts, int* __restrict__ pack_of,
+                                                          const int* lengths, const uint8_t* general,
+                                                          const int* counts, int* __restrict__ pack_of,
                                                           int* __restrict__ row_of) {
   const int b = blockIdx.x;
   griddep_launch_dependents();
@@ -196,7 +195,7 @@ __global__ void __launch_bounds__(1024) prep_pack_kernel(const uint8_t* __restri
 
 // Live tiles of the packed rows: tiles 0 .. ceil(T_v/128)-1, and row_of = -1
 // for the packed rows of the last tile past T_v.  One block.
-__global__ void prep_pack_tiles_kernel(const int* __restrict__ counts, int B, int* __restrict__ row_of,
+__global__ void prep_pack_tiles_kernel(const int* counts, int B, int* __restrict__ row_of,
                                        int* __restrict__ tile_list, int* __restrict__ n_live,
                                        uint8_t* __restrict__ tile_live, int n_tiles_all) {
   griddep_launch_dependents();
@@ -231,7 +230,7 @@ struct RowValidity {
     if (row >= M) return false;
     const int b = (int)(row / S);
     const int n = (int)(row - (long long)b * S);
-    if (n >= __ldg(lengths + b)) return false;
+    if (n >= lengths[b]) return false;
     return mask == nullptr || __ldg(mask + row) != 0;
   }
 };
@@ -240,10 +239,10 @@ struct RowValidity {
 // Invalid rows inside live tiles (or every invalid row when ALL_ROWS) are
 // written as zeros; rows of dead tiles are skipped.
 template <int VPL, bool OUT_F16, bool ALL_ROWS>
-__global__ void __launch_bounds__(256) layernorm_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
+__global__ void __launch_bounds__(256) layernorm_kernel(const float* x, const float* __restrict__ gamma,
                                                         const float* __restrict__ beta, void* __restrict__ out,
                                                         int d, float eps, RowValidity valid,
-                                                        const uint8_t* __restrict__ tile_live) {
+                                                        const uint8_t* tile_live) {
   griddep_launch_dependents();
   griddep_wait();
   const long long row = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -252,7 +251,7 @@ __global__ void __launch_bounds__(256) layernorm_kernel(const float* __restrict_
   const bool ok = valid(row);
   if (!ok && (valid.pack_of != nullptr || (!ALL_ROWS && tile_live[row / kTileRows] == 0))) return;
   // output row: issued now, used only by the stores at the end
-  const long long orow = valid.pack_of != nullptr ? (long long)__ldg(valid.pack_of + row) : row;
+  const long long orow = valid.pack_of != nullptr ? (long long)valid.pack_of[row] : row;
   const int nvec = d >> 2;
   float4 v[VPL];
   if (ok) {

@@ -249,17 +249,21 @@ def test_dependent_launch_changes_no_bit(shape):
     cfg = EncoderShape(b, n, d, h, f, L, True)
     oracle, cand = _models(cfg, 1.0)
     x, mask = generate_random_case(cfg, DEV, torch.float32, 33, pr)
+    short = mask.clone()
+    short[:, n // 3:] = False  # other lengths, tile counts and packing maps on the same workspace
     try:
         outs = []
         for mode in (1, 0, 1):
             _lib.call("tj_set_pdl", mode)
             with torch.inference_mode():
-                outs.append(cand(x, mask).clone())
+                outs.append((cand(x, mask).clone(), cand(x, short).clone()))
             torch.cuda.synchronize(DEV)
             assert cand.device_error() == 0
     finally:
         _lib.call("tj_set_pdl", -1)
-    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[0], outs[2])
+    for k in range(2):
+        assert torch.equal(outs[0][k], outs[1][k]) and torch.equal(outs[0][k], outs[2][k])
+    outs = [o[0] for o in outs]
     with torch.inference_mode():
         _assert_pass(oracle(x, mask), outs[0], mask, cand)
 

@@ -67,3 +67,35 @@ def test_noalloc_forward_rejects_oversize_shape():
     status, _ = _noalloc(model, x, None)
     assert status == 2  # TJ_ERR_UNSUPPORTED
     assert b"scratch" in _lib.load().tj_last_error()
+
+
+def test_noalloc_forward_captures_without_allocating():
+    """The entry point's promise, checked directly: once the first call has
+    resolved the scratch array's address, a call captured into a CUDA graph
+    with capture_error_mode="global" (where any cudaMalloc, from any thread,
+    invalidates the capture) succeeds, and replaying it gives the eager
+    result bit for bit."""
+    cfg = EncoderShape(2, 384, 256, 8, 1024, 2, True)
+    model = CANDIDATE.model_factory(cfg)
+    model.load_state_dict(seeded_encoder(cfg, 77).state_dict(), strict=True)
+    model = model.to(DEV).eval()
+    model.attention_route = "exact"
+    x, m = generate_random_case(cfg, DEV, torch.float32, 77, 0.4)
+    with torch.inference_mode():
+        status, eager = _noalloc(model, x, m)
+        torch.cuda.synchronize()
+        assert status == _lib.TJ_OK, _lib.load().tj_last_error()
+        handle = model._ensure_packed(x.device)
+        out = torch.zeros_like(x)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, capture_error_mode="global"):
+            stream = torch.cuda.current_stream(x.device)
+            status = _lib.load().tj_forward_noalloc(handle.ptr, x.data_ptr(), m.data_ptr(), out.data_ptr(),
+                                                    x.shape[0], x.shape[1], _lib.ROUTE_EXACT,
+                                                    ctypes.c_void_p(stream.cuda_stream))
+        assert status == _lib.TJ_OK, _lib.load().tj_last_error()
+        graph.replay()
+        torch.cuda.synchronize()
+    assert model.device_error() == 0
+    assert torch.equal(out, eager)
+    del graph
