@@ -16,8 +16,9 @@ into rank 0's [B, N, d] buffer, ``value_no_gather`` without it).  ``e2e`` =
 the latency of one call through the public API
 (``DispatchingTransformer.forward``) with the host->device copy of x (the
 valid rows of each right-padded sample, as ``forward_host`` uploads them)
-and the mask from pinned memory and the device->host copy of the whole
-output inside the timed region; ``e2e.pipelined_ms`` = the per-step time when consecutive
+and the mask from pinned memory and the device->host copy of the output
+(its valid rows; the padded rows, exactly 0, are zeroed on the host) inside
+the timed region; ``e2e.pipelined_ms`` = the per-step time when consecutive
 calls overlap their copies.  ``roofline`` = the dominant kernel class,
 measured live with per-launch CUDA events (libtj's profiler) in a second
 pass over the same inputs, against the measured burst peak.
@@ -49,7 +50,7 @@ sys.path.insert(0, str(ROOT))
 
 from techjam_b200 import _lib  # noqa: E402
 from techjam_b200.dispatcher import DispatchingTransformer  # noqa: E402
-from techjam_b200.model import copy_valid_rows, prefix_lengths  # noqa: E402
+from techjam_b200.model import copy_valid_rows, download_valid_rows, prefix_lengths  # noqa: E402
 from techjam_b200.harness import CONFIGS, generate_random_case, seeded_model, valid_lengths, work  # noqa: E402
 from techjam_b200.sharding import (SeqShardComm, forward_seqshard, gather_batch_outputs, sample_owners,  # noqa: E402
                                    shard_samples, take_tokens, token_ranges)
@@ -329,7 +330,9 @@ def end_to_end(fwd, x, mask, steps, warmup, stream, barrier):
     step's copies on the device with CUDA events.  The copy-in is what
     ``B200Transformer.forward_host`` uploads: each right-padded sample's
     valid rows (``tj_copy_valid_rows``; the forward never reads padded rows)
-    and the mask; the copy-out is the whole [B, N, d] result.
+    and the mask; the copy-out is each sample's valid rows of the result,
+    with its padded rows zeroed on the host meanwhile (all rows for a
+    non-prefix mask).
     """
     dev = x.device
     xh = [x.cpu().pin_memory() for _ in range(2)]
@@ -342,7 +345,13 @@ def end_to_end(fwd, x, mask, steps, warmup, stream, barrier):
     row_bytes = x.shape[2] * 4
     h2d_bytes = int((sum(lengths) * row_bytes if lengths is not None else x.numel() * 4)
                     + (0 if mask is None else mask.numel()))
-    d2h_bytes = int(x.numel() * 4)
+    d2h_bytes = int(sum(lengths) * row_bytes if lengths is not None else x.numel() * 4)
+
+    def download(k, y):
+        if lengths is not None:
+            download_valid_rows(outh[k], y, lengths, torch.cuda.current_stream(dev))
+        else:
+            outh[k].copy_(y, non_blocking=True)
 
     def upload(k):
         if lengths is not None:
@@ -355,14 +364,14 @@ def end_to_end(fwd, x, mask, steps, warmup, stream, barrier):
     # serial
     for _ in range(max(1, warmup)):
         upload(0)
-        outh[0].copy_(fwd(xd[0], md[0]), non_blocking=True)
+        download(0, fwd(xd[0], md[0]))
     torch.cuda.synchronize(dev)
     barrier()
     s0, e0 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     s0.record(stream)
     for _ in range(steps):
         upload(0)
-        outh[0].copy_(fwd(xd[0], md[0]), non_blocking=True)
+        download(0, fwd(xd[0], md[0]))
     e0.record(stream)
     torch.cuda.synchronize(dev)
     serial_ms = s0.elapsed_time(e0) / steps
@@ -398,7 +407,7 @@ def end_to_end(fwd, x, mask, steps, warmup, stream, barrier):
             out_ready[k].record(stream)
             with torch.cuda.stream(s_out):
                 s_out.wait_event(out_ready[k])
-                outh[k].copy_(y, non_blocking=True)
+                download(k, y)
                 y.record_stream(s_out)
                 out_free[k].record(s_out)
             pending[k] = y

@@ -92,6 +92,19 @@ def copy_valid_rows(dst: torch.Tensor, src: torch.Tensor, lengths: List[int], st
     return sum(lengths) * row_bytes
 
 
+def download_valid_rows(out_host: torch.Tensor, y: torch.Tensor, lengths: List[int], stream=None) -> int:
+    """Copy each sample's valid rows of the device result ``y`` into
+    ``out_host`` (asynchronously; pinned memory) and zero its padded rows on
+    the host meanwhile -- they are exactly 0 by the reference's contract, so
+    they need not cross the host link.  Returns the bytes copied."""
+    nbytes = copy_valid_rows(out_host, y, lengths, stream)
+    seq_len = y.shape[1]
+    for b, n in enumerate(lengths):
+        if n < seq_len:
+            out_host[b, n:].zero_()
+    return nbytes
+
+
 class _Handle:
     """Owns one ``TjModel*`` on one device; destroyed with its Python owner."""
 
@@ -287,9 +300,11 @@ class B200Transformer(nn.Module):
         (the reference generator's) each sample's valid rows, else every row;
         the mask itself; runs ``forward`` on the model's CUDA device (with its
         CUDA graph when enabled: the device staging buffers are reused per
-        shape) and copies the whole [B, N, d] FP32 result back, padded rows
-        0.  Pinned ``x`` / ``out`` let the copies run asynchronously.  Returns
-        once the result is in host memory.
+        shape) and copies back the valid rows of the [B, N, d] FP32 result,
+        zeroing the padded rows on the host while the GPU works (every row
+        for a mask that is not a right-padded prefix).  Pinned ``x`` / ``out``
+        let the copies run asynchronously.  Returns once the result is in
+        host memory.
         """
         if x.device.type != "cpu" or x.ndim != 3 or x.shape[-1] != self.config.d_model:
             raise ValueError(f"x must be a host tensor [B, N, {self.config.d_model}]")
@@ -321,7 +336,10 @@ class B200Transformer(nn.Module):
         y = self.forward(xd, md)
         if out is None:
             out = torch.empty((batch, seq_len, d), dtype=torch.float32, pin_memory=True)
-        out.copy_(y, non_blocking=True)
+        if lengths is not None:
+            download_valid_rows(out, y, lengths)
+        else:
+            out.copy_(y, non_blocking=True)
         torch.cuda.current_stream(device).synchronize()
         return out if x.dtype == torch.float32 else out.to(x.dtype)
 

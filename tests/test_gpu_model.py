@@ -287,7 +287,7 @@ def test_forward_host_uploads_valid_rows_only():
         mask2[:, 100:] = False
         ref2 = cand(x, mask2).cpu()
         assert torch.equal(cand.forward_host(xh, mask2.cpu(), out=out), ref2)
-        assert torch.all(out[~mask2.cpu()] == 0)
+        assert torch.all(out[~mask2.cpu()] == 0)  # rows that held results before are zeroed
         # a mask with holes: every row is uploaded
         mask3 = mask.clone()
         mask3[0, 3] = False
