@@ -248,6 +248,16 @@ TJ_API int tj_attention_f16(const void* q, const void* k, const void* v, void* c
                      int head_dim, int causal, const int* lengths, const uint8_t* mask, const uint8_t* general,
                      int* err, int* sched, void* stream);
 
+/* The attention of one sequence shard, as tj_forward_seqshard runs it after
+   its K/V all-gather (no counterpart in the reference; exposed so the shard
+   layouts can be checked on one GPU): causal, unpadded; q is shard `rank`'s
+   queries fp16 [B,H,seq_local,hd] in local row order, k_all / v_all hold
+   every shard's keys / values [world][B][H][seq_local][hd], lengths[b] = the
+   global sequence length, layout a TjShardLayout; ctx as tj_attention_f16. */
+TJ_API int tj_attention_shard_f16(const void* q, const void* k_all, const void* v_all, void* ctx, int batch,
+                                  int heads, int seq_local, int head_dim, const int* lengths, const uint8_t* general,
+                                  int* err, int* sched, int rank, int world, int layout, void* stream);
+
 /* ---- sequence sharding over NCCL (one process per GPU) ----------------- */
 
 typedef struct TjComm TjComm;

@@ -59,6 +59,8 @@ SIGNATURES = {
     "tj_device_error": (c_int, [c_void_p, POINTER(c_int)]),
     "tj_set_wait_limit": (c_int, [ctypes.c_ulonglong]),
     "tj_set_pdl": (c_int, [c_int]),
+    "tj_attention_shard_f16": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p,
+                                       c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]),
     "tj_copy_valid_rows": (c_int, [c_void_p, c_void_p, POINTER(c_int), c_int, c_int, c_size_t, c_void_p]),
     "tj_wait_selftest": (c_int, [c_void_p, c_void_p, c_void_p]),
     "tj_profile_begin": (c_int, [c_void_p, c_int]),

@@ -1111,6 +1111,33 @@ int tj_attention_f16(const void* q, const void* k, const void* v, void* ctx, int
   return launch_attention(q, k, v, hd, p, B, static_cast<cudaStream_t>(stream));
 }
 
+int tj_attention_shard_f16(const void* q, const void* k_all, const void* v_all, void* ctx, int B, int H, int S_loc,
+                           int hd, const int* lengths, const uint8_t* general, int* err, int* sched, int rank,
+                           int world, int layout, void* stream) {
+  if (!q || !k_all || !v_all || !ctx || !lengths || !general || !err) return fail(TJ_ERR_INVALID, "null argument");
+  if (world <= 0 || rank < 0 || rank >= world) return fail(TJ_ERR_INVALID, "rank %d of %d", rank, world);
+  if (layout != TJ_SHARD_CONTIGUOUS && layout != TJ_SHARD_ZIGZAG) return fail(TJ_ERR_INVALID, "unknown layout %d", layout);
+  if (S_loc <= 0 || S_loc % (layout == TJ_SHARD_ZIGZAG ? 512 : 128) != 0)
+    return fail(TJ_ERR_UNSUPPORTED, "seq_local %d must be a multiple of %d", S_loc, layout == TJ_SHARD_ZIGZAG ? 512 : 128);
+  tj::AttnParams p{};
+  p.lengths = lengths; p.mask = nullptr; p.general = general; p.ctx = static_cast<__half*>(ctx);
+  p.S = S_loc; p.H = H; p.d_model = H * hd; p.causal = 1;
+  p.scale_log2 = (float)(1.0 / std::sqrt((double)hd) * 1.4426950408889634);
+  p.err = err;
+  p.kv_shard = S_loc;
+  p.kv_shards = world;
+  if (layout == TJ_SHARD_ZIGZAG) {
+    p.zz_chunk = S_loc / 2;
+    p.q_pos0 = rank * p.zz_chunk;
+    p.q_pos1 = (2 * world - 1 - rank) * p.zz_chunk;
+  } else {
+    p.q_pos0 = rank * S_loc;
+  }
+  p.B = B;
+  p.sched = sched;
+  return launch_attention(q, k_all, v_all, hd, p, B, static_cast<cudaStream_t>(stream));
+}
+
 }  // extern "C"
 
 // ------------------------------------------------------------------ sequence-sharded forward (NCCL)

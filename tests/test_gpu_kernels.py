@@ -182,3 +182,39 @@ def test_attention_scheduler_static_equals_dynamic(b, h, n, hd, causal):
     ref = _attn_ref(q.cpu(), k.cpu(), v.cpu(), mask, causal)
     rows_ok = mask.reshape(-1)
     torch.testing.assert_close(static.float().cpu()[rows_ok], ref[rows_ok], atol=4e-3, rtol=1e-2)
+
+
+@pytest.mark.parametrize("hd", [32, 64, 128])
+@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("layout", ["contiguous", "zigzag"])
+def test_sharded_attention_layouts_on_one_gpu(hd, world, layout):
+    """The sequence-sharded attention (local queries at their global positions
+    over every shard's K/V, as the multi-GPU forward runs it after its K/V
+    all-gather), emulated rank by rank on one GPU: each shard's context rows
+    equal the unsharded causal attention's rows bit for bit, for both token
+    layouts and every head_dim (persistent kernel for <= 64, per-pair for 128)."""
+    from techjam_b200.sharding import token_ranges
+    b, h, s = 2, 2, world * 512
+    gen = torch.Generator(device=DEV).manual_seed(hd * 10 + world)
+    q, k, v = (torch.randn(b, h, s, hd, device=DEV, generator=gen).half() for _ in range(3))
+    full_info = ops.prepare_mask(None, b, s, DEV)
+    ref = ops.attention(q, k, v, full_info, causal=True)  # [b*s, h*hd]
+    lengths = torch.full((b,), s, dtype=torch.int32, device=DEV)
+    general = torch.zeros(b, dtype=torch.uint8, device=DEV)
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    sched = torch.zeros(2, dtype=torch.int32, device=DEV)
+    parts = [token_ranges(s, world, r, layout) for r in range(world)]
+    rows = [torch.cat([torch.arange(rg.start, rg.stop) for rg in rs]).to(DEV) for rs in parts]
+    k_all = torch.stack([k[:, :, idx] for idx in rows]).contiguous()
+    v_all = torch.stack([v[:, :, idx] for idx in rows]).contiguous()
+    s_loc = s // world
+    for r in range(world):
+        q_loc = q[:, :, rows[r]].contiguous()
+        ctx = torch.zeros(b * s_loc, h * hd, dtype=torch.float16, device=DEV)
+        _lib.call("tj_attention_shard_f16", q_loc.data_ptr(), k_all.data_ptr(), v_all.data_ptr(), ctx.data_ptr(),
+                  b, h, s_loc, hd, lengths.data_ptr(), general.data_ptr(), err.data_ptr(), sched.data_ptr(), r, world,
+                  1 if layout == "zigzag" else 0, torch.cuda.current_stream().cuda_stream)
+        torch.cuda.synchronize()
+        assert int(err.item()) == 0
+        want = ref.view(b, s, h * hd)[:, rows[r]].reshape(b * s_loc, h * hd)
+        assert torch.equal(ctx, want), f"rank {r}: max diff {(ctx.float() - want.float()).abs().max().item()}"
