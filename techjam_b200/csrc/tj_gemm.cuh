@@ -138,10 +138,23 @@ TJ_DEV bool f16_epilogue(const GemmParams& p, uint32_t taddr, int row0, int colh
       }
     }
   }
+  // the bias of the next chunk is loaded one chunk ahead (chunk 0's under
+  // the accumulator wait), so its latency hides behind the current chunk
+  float4 bias_next[8];
+  auto load_bias = [&](int c) {
+    if (colh + c * 32 >= p.N) return;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) bias_next[j] = __ldg(reinterpret_cast<const float4*>(p.bias + colh + c * 32) + j);
+  };
+  if (live) load_bias(0);
   if (!wait_acc()) return false;
   tc_fence_after();
 #pragma unroll
   for (int c = 0; c < kChunks; ++c) {
+    float4 bias_cur[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) bias_cur[j] = bias_next[j];
+    if (live && c + 1 < kChunks) load_bias(c + 1);
     uint32_t acc[32];
     tmem_ld32(taddr + c * 32, acc);
     tmem_ld_wait();
@@ -151,7 +164,7 @@ TJ_DEV bool f16_epilogue(const GemmParams& p, uint32_t taddr, int row0, int colh
     if (my_valid) {
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const float4 bb = __ldg(reinterpret_cast<const float4*>(p.bias + col0) + j);
+        const float4 bb = bias_cur[j];
         float v0 = __uint_as_float(acc[4 * j]) + bb.x, v1 = __uint_as_float(acc[4 * j + 1]) + bb.y;
         float v2 = __uint_as_float(acc[4 * j + 2]) + bb.z, v3 = __uint_as_float(acc[4 * j + 3]) + bb.w;
         if constexpr (EPI == kEpiGelu) {
@@ -256,9 +269,11 @@ TJ_DEV bool resid_epilogue(const GemmParams& p, uint32_t taddr, int row0, int co
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
   }
   float4 res[2][8];
+  float4 bias4[2];  // this lane's 4 bias columns of the chunk, loaded with its residual
   auto prefetch = [&](int c, float4 (&r)[8]) {
     const int col = colh + c * 32 + c4;
     if (colh + c * 32 >= p.N) return;
+    bias4[c & 1] = __ldg(reinterpret_cast<const float4*>(p.bias + col));
 #pragma unroll
     for (int i = 0; i < 8; ++i)
       if ((valid >> i) & 1u) r[i] = *reinterpret_cast<const float4*>(p.resid + (size_t)prow[i] * p.N + col);
@@ -274,7 +289,7 @@ TJ_DEV bool resid_epilogue(const GemmParams& p, uint32_t taddr, int row0, int co
     tmem_ld_wait();
     const int col0 = colh + c * 32;
     if (!live || col0 >= p.N) continue;  // warp-uniform
-    const float4 b4 = __ldg(reinterpret_cast<const float4*>(p.bias + col0 + c4));
+    const float4 b4 = bias4[c & 1];
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       if ((lane >> 4) == h) {
