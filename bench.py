@@ -61,7 +61,7 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 # kernel, from the ncu captures summarised in profiles/, keyed (workload, kernel class).
 NCU_TRAFFIC_BYTES: dict = {
     ("C2", "attention"): 205261312 + 22824704,      # attn_fwd_persistent_kernel<64> (profiles/c2_kernels_full.md)
-    ("C2", "gemm_ffn_in"): 54178816 + 132079872,    # gemm_tc2_kernel<1>
+    ("C2", "gemm_ffn_in"): 54178560 + 136292352,    # gemm_tc2_kernel<1>
 }
 CPU_DENSE_MAX = 8192  # longest sample the CPU baseline runs through the dense model
 # Whole batches whose dense [B, H, N, N] FP32 scores fit comfortably in host memory
