@@ -126,15 +126,24 @@ TJ_DEV bool f16_epilogue(const GemmParams& p, uint32_t taddr, int row0, int colh
   const bool my_valid = live && row_is_valid(p, row0 + lane);  // this thread's accumulator row
   const int piece = lane & 3;
   uint32_t in_m = 0;  // bit 2h+i: store-side row row0 + 16h + 8i + lane/4 is < M
-  int srow[4];         // QKV: that row's padded token position (fetched under the main loop)
+  // QKV: element offset of that row's token (b, n) in head 0 of Q/K/V
+  // [B, H, seq, hd], or -1 (a packed row past the last valid token); worked
+  // out under the main loop so the stores need no division
+  long long tok_ofs[4];
   if (live) {
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
       const int row = row0 + 8 * k + (lane >> 2);
-      srow[k] = row;
+      tok_ofs[k] = -1;
       if (row < p.M) {
         in_m |= 1u << k;
-        if (EPI == kEpiQKV && p.row_of != nullptr) srow[k] = p.row_of[row];
+        if constexpr (EPI == kEpiQKV) {
+          const int pr = p.row_of != nullptr ? p.row_of[row] : row;
+          if (pr >= 0) {
+            const int b = pr / p.seq;
+            tok_ofs[k] = ((long long)b * p.heads * p.seq + (pr - b * p.seq)) * p.head_dim;
+          }
+        }
       }
     }
   }
@@ -186,7 +195,7 @@ TJ_DEV bool f16_epilogue(const GemmParams& p, uint32_t taddr, int row0, int colh
       const int hc = col0 - which * p.d_model;
       head = hc / p.head_dim;
       dim0 = hc - head * p.head_dim;
-      col_base = which == 0 ? p.q : (which == 1 ? p.k : p.v);
+      col_base = (which == 0 ? p.q : (which == 1 ? p.k : p.v)) + (size_t)head * p.seq * p.head_dim + dim0;
     } else {
       col_base = p.out16 + col0;
     }
@@ -208,12 +217,8 @@ TJ_DEV bool f16_epilogue(const GemmParams& p, uint32_t taddr, int row0, int colh
           if constexpr (EPI == kEpiQKV) {
             // packed rows scatter to their token's padded position; a packed
             // row past the last valid token has none
-            const int pr = srow[2 * h + i];
-            if (pr >= 0) {
-              const int b = pr / p.seq;
-              const int n = pr - b * p.seq;
-              dst = col_base + (((size_t)b * p.heads + head) * p.seq + n) * p.head_dim + dim0;
-            }
+            const long long ofs = tok_ofs[2 * h + i];
+            if (ofs >= 0) dst = col_base + ofs;
           } else {
             dst = col_base + (size_t)row * p.N;
           }
