@@ -60,7 +60,7 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 # dram__bytes_read.sum + dram__bytes_write.sum of one launch of the workload's dominant
 # kernel, from the ncu captures summarised in profiles/, keyed (workload, kernel class).
 NCU_TRAFFIC_BYTES: dict = {
-    ("C2", "attention"): 205261312 + 22824704,      # attn_fwd_persistent_kernel<64> (profiles/c2_kernels_full.md)
+    ("C2", "attention"): 206195712 + 22177024,      # attn_fwd_persistent_kernel<64> (profiles/c2_kernels_full.md)
     ("C2", "gemm_ffn_in"): 54178560 + 136292352,    # gemm_tc2_kernel<1>
 }
 CPU_DENSE_MAX = 8192  # longest sample the CPU baseline runs through the dense model
