@@ -364,17 +364,17 @@ int launch_layernorm(const float* x, const float* g, const float* b, void* out, 
                      float eps, const tj::RowValidity& rv, const uint8_t* tile_live, cudaStream_t st) {
   if (d % 4 != 0 || d > 4096) return fail(TJ_ERR_UNSUPPORTED, "LayerNorm width %d (need multiple of 4, <= 4096)", d);
   if (rv.M == 0) return TJ_OK;
-  const int warps = 8;
+  const int warps = 4;
   const long long blocks = (rv.M + warps - 1) / warps;
   if (blocks > 0x7fffffffLL) return fail(TJ_ERR_UNSUPPORTED, "too many rows");
   const int vpl = (d / 4 + 31) / 32;
 #define TJ_LN(V)                                                                                              \
   if (f16) {                                                                                                  \
-    if (all_rows) TJ_CHECK(launch_pdl(tj::layernorm_kernel<V, true, true>, dim3((unsigned)blocks), dim3(256), 0, st, x, g, b, out, d, eps, rv, tile_live)); \
-    else TJ_CHECK(launch_pdl(tj::layernorm_kernel<V, true, false>, dim3((unsigned)blocks), dim3(256), 0, st, x, g, b, out, d, eps, rv, tile_live));         \
+    if (all_rows) TJ_CHECK(launch_pdl(tj::layernorm_kernel<V, true, true>, dim3((unsigned)blocks), dim3(32 * warps), 0, st, x, g, b, out, d, eps, rv, tile_live)); \
+    else TJ_CHECK(launch_pdl(tj::layernorm_kernel<V, true, false>, dim3((unsigned)blocks), dim3(32 * warps), 0, st, x, g, b, out, d, eps, rv, tile_live));         \
   } else {                                                                                                    \
-    if (all_rows) TJ_CHECK(launch_pdl(tj::layernorm_kernel<V, false, true>, dim3((unsigned)blocks), dim3(256), 0, st, x, g, b, out, d, eps, rv, tile_live)); \
-    else TJ_CHECK(launch_pdl(tj::layernorm_kernel<V, false, false>, dim3((unsigned)blocks), dim3(256), 0, st, x, g, b, out, d, eps, rv, tile_live));        \
+    if (all_rows) TJ_CHECK(launch_pdl(tj::layernorm_kernel<V, false, true>, dim3((unsigned)blocks), dim3(32 * warps), 0, st, x, g, b, out, d, eps, rv, tile_live)); \
+    else TJ_CHECK(launch_pdl(tj::layernorm_kernel<V, false, false>, dim3((unsigned)blocks), dim3(32 * warps), 0, st, x, g, b, out, d, eps, rv, tile_live));        \
   }
   if (vpl <= 1) { TJ_LN(1) }
   else if (vpl <= 2) { TJ_LN(2) }
